@@ -1,0 +1,192 @@
+// ffa_capi.cu — the C ABI of libffa_sm100.so (declared in include/ffa.h).
+//
+// This is the library's single translation unit: it includes every kernel header, so
+// the device status word `ffa::g_status` has exactly one definition.  The entry points
+// validate their arguments, build TMA tensor maps and launch on the caller's stream;
+// they never allocate device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "ffa_common.cuh"
+#include "ffa_fwd.cuh"
+#include "ffa_bwd.cuh"
+#include "ffa_aux.cuh"
+
+namespace ffa {
+
+namespace {
+thread_local int t_last_code = FFA_OK;
+thread_local char t_last_msg[256] = "";
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+int set_error(int code, const char* msg) {
+  t_last_code = code;
+  std::snprintf(t_last_msg, sizeof(t_last_msg), "%s", msg ? msg : "");
+  return code;
+}
+
+int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,
+                  long long stride_s, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(FFA_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_s) * 2, static_cast<cuuint64_t>(stride_bh) * 2};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    return set_error(FFA_ERR_INVALID, buf);
+  }
+  return FFA_OK;
+}
+
+// Shape / stride / alignment checks shared by the entry points.
+static int check_common(int BH, int S, int D, long long stride_bh, long long stride_s) {
+  if (BH < 0 || S < 0) return set_error(FFA_ERR_INVALID, "BH and S must be non-negative");
+  if (D != 64 && D != 128) return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
+  if (stride_s < D || stride_s % 8 != 0) return set_error(FFA_ERR_INVALID, "stride_s must be >= D and a multiple of 8");
+  if (BH > 1 && (stride_bh < static_cast<long long>(S) * stride_s || stride_bh % 8 != 0))
+    return set_error(FFA_ERR_INVALID, "stride_bh must be >= S*stride_s and a multiple of 8");
+  return FFA_OK;
+}
+
+}  // namespace ffa
+
+using namespace ffa;
+
+extern "C" {
+
+int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH, int S, int D,
+            long long stride_bh, long long stride_s, double scale, int causal, void* stream) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !o) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  FwdArgs a{q, k, v, o, lse, BH, S, D, stride_bh, stride_s, scale, causal};
+  return launch_fwd(a, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_bwd_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D, long long stride_bh,
+                       long long stride_s, void* stream) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!o || !dout || !delta) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(o) || !aligned16(dout)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  return launch_preprocess(o, dout, delta, BH, S, D, stride_bh, stride_s, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
+            float* delta_ws, void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh,
+            long long stride_s, double scale, int causal, void* stream) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !o || !dout || !lse || !delta_ws || !dq || !dk || !dv)
+    return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  for (const void* p : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                        static_cast<const void*>(dv)})
+    if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  BwdArgs a{q, k, v, o, dout, lse, delta_ws, dq, dk, dv, BH, S, D, stride_bh, stride_s, scale, causal};
+  return launch_bwd(a, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,
+                  int first, void* stream) {
+  if (rows < 0 || D <= 0 || D > 128 || D % 4 != 0) return set_error(FFA_ERR_INVALID, "bad rows / D for merge");
+  if (rows == 0) return FFA_OK;
+  if (!acc || !acc_lse || !part || !part_lse) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(acc) || (reinterpret_cast<uintptr_t>(part) & 7u))
+    return set_error(FFA_ERR_INVALID, "acc must be 16-byte and part 8-byte aligned");
+  return launch_lse_merge(acc, acc_lse, part, part_lse, rows, D, first, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_last_error(char* buf, int n) {
+  if (buf && n > 0) {
+    std::strncpy(buf, t_last_msg, static_cast<size_t>(n - 1));
+    buf[n - 1] = '\0';
+  }
+  return t_last_code;
+}
+
+int ffa_device_status(unsigned int* out4) {
+  if (!out4) return set_error(FFA_ERR_INVALID, "null output");
+  if (cudaDeviceSynchronize() != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaDeviceSynchronize failed");
+  unsigned int host[4] = {0, 0, 0, 0};
+  if (cudaMemcpyFromSymbol(host, g_status, sizeof(host)) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "reading the device status word failed");
+  const unsigned int zero[4] = {0, 0, 0, 0};
+  if (cudaMemcpyToSymbol(g_status, zero, sizeof(zero)) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "clearing the device status word failed");
+  std::memcpy(out4, host, sizeof(host));
+  if (host[0] != 0 || host[1] != 0 || host[2] != 0) {
+    char buf[128];
+    std::snprintf(buf, sizeof(buf), "device wait timeout: site 0x%x, %u waits, %u drains", host[0], host[1], host[2]);
+    return set_error(FFA_ERR_DEVICE, buf);
+  }
+  return FFA_OK;
+}
+
+const char* ffa_version(void) { return "0.2.0+sm100a"; }
+
+}  // extern "C"
+
+namespace ffa {
+
+int launch_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D, long long stride_bh,
+                      long long stride_s, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(BH) * S;
+  const int rows_per_block = 256 / (D / 8);
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  const int grid = static_cast<int>(blocks < 148 * 16 ? blocks : 148 * 16);
+  if (D == 128)
+    ffa_preprocess_kernel<128><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(o),
+                                                          static_cast<const __nv_bfloat16*>(dout), delta, BH, S,
+                                                          stride_bh, stride_s);
+  else
+    ffa_preprocess_kernel<64><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(o),
+                                                         static_cast<const __nv_bfloat16*>(dout), delta, BH, S,
+                                                         stride_bh, stride_s);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
+  return FFA_OK;
+}
+
+int launch_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,
+                     int first, cudaStream_t stream) {
+  const long long blocks = (rows + 7) / 8;
+  const int grid = static_cast<int>(blocks < 148 * 16 ? blocks : 148 * 16);
+  ffa_lse_merge_kernel<<<grid, 256, 0, stream>>>(acc, acc_lse, static_cast<const __nv_bfloat16*>(part), part_lse,
+                                                 rows, D, first);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
+  return FFA_OK;
+}
+
+}  // namespace ffa

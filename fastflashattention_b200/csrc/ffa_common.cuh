@@ -1,0 +1,72 @@
+// ffa_common.cuh — shared host/device declarations of the attention library.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "../../include/ffa.h"
+#include "sm100.cuh"
+
+namespace ffa {
+
+// log2(e), the base change folded into the softmax scale (reference _kernel.py:40)
+constexpr double kLog2e = 1.4426950408889634;
+
+// ids of the waits that can time out (recorded in g_status[0])
+enum : unsigned int {
+  kErrFwdProducer = 0x101,
+  kErrFwdMma = 0x102,
+  kErrFwdSoftmax = 0x103,
+  kErrBwdProducer = 0x201,
+  kErrBwdMma = 0x202,
+  kErrBwdCompute = 0x203,
+  kErrDqProducer = 0x301,
+  kErrDqMma = 0x302,
+  kErrDqCompute = 0x303,
+};
+
+struct FwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  int BH, S, D;
+  long long stride_bh, stride_s;
+  double scale;
+  int causal;
+};
+
+struct BwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  float* delta;
+  void* dq;
+  void* dk;
+  void* dv;
+  int BH, S, D;
+  long long stride_bh, stride_s;
+  double scale;
+  int causal;
+};
+
+// host helpers (ffa_capi.cu)
+int set_error(int code, const char* msg);
+// 3-D tensor map over a [BH, S, D] bf16 tensor: box = 64 columns x `box_rows` rows x 1
+// slice, 128-byte swizzle (the layout the tcgen05 descriptors in sm100.cuh expect).
+int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,
+                  long long stride_s, int box_rows = 128);
+
+int launch_fwd(const FwdArgs& a, cudaStream_t stream);
+int launch_bwd(const BwdArgs& a, cudaStream_t stream);
+int launch_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D, long long stride_bh,
+                      long long stride_s, cudaStream_t stream);
+int launch_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,
+                     int first, cudaStream_t stream);
+
+}  // namespace ffa

@@ -1,0 +1,379 @@
+// ffa_fwd.cuh — exact bf16 attention forward for sm_100a.
+//
+// Computes, per (batch*head) slice and per query row i,
+//   O_i   = sum_j softmax_j( scale * q_i . k_j  [j <= i if causal] ) v_j
+//   LSE_i = m_i + log2(l_i)          (base-2 log-sum-exp of scale*log2(e)*q.k)
+// which is the contract of the reference forward `_fastflash_fwd`
+// (fastflash_attention/_kernel.py:194-279): exp2 with scale*log2(e) folded into the
+// scores, fp32 online softmax, P rounded to bf16 before the P.V product (:245), the
+// fully-masked-row guards (:260, :269, :276) and the base-2 LSE (:274-279).
+//
+// B200 design (one CTA = 256 query rows = two 128-row tiles, one CTA per SM):
+//   warps 0-3   softmax warpgroup for tile 0 (thread t owns row t: TMEM lane t)
+//   warps 4-7   softmax warpgroup for tile 1
+//   warp  8     TMA producer: Q0/Q1 once, then K_j, V_j through a 3-slot smem ring
+//   warp  9     MMA issuer (one thread): S_i = Q_i K_j^T  and  O_i += P_i V_j
+// TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512).
+// P_i (bf16, two per column) overwrites the first 64 columns of S_i and is the
+// A operand of the P.V MMA straight from tensor memory, so P never touches smem.
+// While warpgroup 0 exponentiates tile 0, the tensor core works on tile 1 and vice
+// versa.  The running max is rescaled lazily: O and l are rescaled only when a row's
+// max grows by more than 2^8, which keeps every P <= 256 (exact in fp32 / bf16 range).
+#pragma once
+#include "ffa_common.cuh"
+
+namespace ffa {
+
+namespace fwd {
+constexpr int BM = 128;            // rows per Q tile (TMEM lanes)
+constexpr int BN = 128;            // keys per K/V tile
+constexpr int STAGES = 3;          // K/V smem ring slots
+constexpr int NTHREADS = 320;
+constexpr int PRODUCER_WARP = 8;
+constexpr int MMA_WARP = 9;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+template <int D>
+struct Layout {
+  static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row bf16 tile
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
+  // barriers: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain
+  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1;
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;  // tmem base, abort flag
+  static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;  // + alignment slack
+};
+}  // namespace fwd
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(fwd::NTHREADS, 1)
+    ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ O,
+                   float* __restrict__ LSE, int S, long long o_stride_bh, long long o_stride_s,
+                   float scale_log2) {
+  using L = fwd::Layout<D>;
+  constexpr int SLABS = D / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::BAR_OFF;
+  const uint32_t q_full = bar0;
+  auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8 * (1 + fwd::STAGES + s); };
+  auto s_full = [&](int i) { return bar0 + 8 * (1 + 2 * fwd::STAGES + i); };
+  auto p_ready = [&](int i) { return bar0 + 8 * (3 + 2 * fwd::STAGES + i); };
+  auto o_final = [&](int i) { return bar0 + 8 * (5 + 2 * fwd::STAGES + i); };
+  const uint32_t drain_bar = bar0 + 8 * (7 + 2 * fwd::STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_mblk = gridDim.x;
+  // heaviest causal blocks first
+  const int mblk = CAUSAL ? (n_mblk - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y;
+  const int m0 = mblk * 2 * fwd::BM;
+  const int n_kv_all = (S + fwd::BN - 1) / fwd::BN;
+  int n_tiles[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int mi = m0 + i * fwd::BM;
+    if (mi >= S) {
+      n_tiles[i] = 0;
+    } else if (CAUSAL) {
+      n_tiles[i] = min(n_kv_all, (mi + fwd::BM - 1) / fwd::BN + 1);
+    } else {
+      n_tiles[i] = n_kv_all;
+    }
+  }
+  const int n_kv = max(n_tiles[0], n_tiles[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < fwd::STAGES; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full(i), 1);
+      mbar_init(p_ready(i), 128);
+      mbar_init(o_final(i), 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == fwd::MMA_WARP) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == fwd::PRODUCER_WARP && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == fwd::PRODUCER_WARP) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, 2 * L::TILE_BYTES);
+      for (int i = 0; i < 2; ++i)
+        for (int sl = 0; sl < SLABS; ++sl)
+          tma_load_3d(sbase + L::Q_OFF + i * L::TILE_BYTES + sl * 16384, &tm_q, q_full, sl * 64,
+                      m0 + i * fwd::BM, bh, keep);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int which = 0; which < 2; ++which) {
+          const int it = 2 * j + which;
+          const int s = it % fwd::STAGES;
+          if (!mbar_wait(kv_empty(s), ((it / fwd::STAGES) & 1) ^ 1, abort_flag, kErrFwdProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(kv_full(s), L::TILE_BYTES);
+          const CUtensorMap* tm = which ? &tm_v : &tm_k;
+          for (int sl = 0; sl < SLABS; ++sl)
+            tma_load_3d(sbase + L::KV_OFF + s * L::TILE_BYTES + sl * 16384, tm, kv_full(s), sl * 64,
+                        j * fwd::BN, bh, keep);
+          ++issued;
+        }
+      }
+      if (!ok) {
+        // let in-flight copies land before the CTA's shared memory goes away
+        for (int it = max(0, issued - fwd::STAGES); it < issued; ++it)
+          mbar_wait_drain(kv_full(it % fwd::STAGES), (it / fwd::STAGES) & 1);
+      }
+    }
+  } else if (warp == fwd::MMA_WARP) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_bf16(128, fwd::BN, false, false);
+      constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
+      const uint32_t q_addr[2] = {sbase + L::Q_OFF, sbase + L::Q_OFF + L::TILE_BYTES};
+      bool ok = mbar_wait(q_full, 0, abort_flag, kErrFwdMma);
+      int it = 0;
+      auto issue_qk = [&](int i, uint32_t k_addr) {
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          mma_ss(tmem + i * 128, kmajor_desc(q_addr[i], 128, ks), kmajor_desc(k_addr, 128, ks), IDESC_QK,
+                 ks > 0);
+        mma_commit(s_full(i));
+      };
+      auto issue_pv = [&](int i, uint32_t v_addr, int j) {
+#pragma unroll
+        for (int ks = 0; ks < fwd::BN / 16; ++ks)
+          mma_ts(tmem + 256 + i * 128, tmem + i * 128 + ks * 8, mnmajor_desc(v_addr, fwd::BN, ks), IDESC_PV,
+                 (j > 0 || ks > 0) ? 1u : 0u);
+      };
+      // prologue: S_i(0)
+      if (ok && n_kv > 0) {
+        const int s = it % fwd::STAGES;
+        ok = mbar_wait(kv_full(s), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t k_addr = sbase + L::KV_OFF + s * L::TILE_BYTES;
+          if (n_tiles[0] > 0) issue_qk(0, k_addr);
+          if (n_tiles[1] > 0) issue_qk(1, k_addr);
+          mma_commit(kv_empty(s));
+          ++it;
+        }
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int sv = it % fwd::STAGES;
+        if (!(ok = mbar_wait(kv_full(sv), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
+        ++it;
+        const uint32_t v_addr = sbase + L::KV_OFF + sv * L::TILE_BYTES;
+        const bool next = (j + 1 < n_kv);
+        int sk = -1;
+        uint32_t k_addr = 0;
+        // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
+        if (j < n_tiles[0]) {
+          if (!(ok = mbar_wait(p_ready(0), j & 1, abort_flag, kErrFwdMma))) break;
+          tc_fence_after();
+          issue_pv(0, v_addr, j);
+        }
+        if (next) {
+          sk = it % fwd::STAGES;
+          if (!(ok = mbar_wait(kv_full(sk), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
+          tc_fence_after();
+          k_addr = sbase + L::KV_OFF + sk * L::TILE_BYTES;
+          if (j + 1 < n_tiles[0]) issue_qk(0, k_addr);
+        }
+        // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
+        if (j < n_tiles[1]) {
+          if (!(ok = mbar_wait(p_ready(1), j & 1, abort_flag, kErrFwdMma))) break;
+          tc_fence_after();
+          issue_pv(1, v_addr, j);
+        }
+        mma_commit(kv_empty(sv));
+        if (next) {
+          if (j + 1 < n_tiles[1]) issue_qk(1, k_addr);
+          mma_commit(kv_empty(sk));
+          ++it;
+        }
+      }
+      if (ok) {
+        mma_commit(o_final(0));
+        mma_commit(o_final(1));
+      }
+      // every issued MMA has finished before TMEM is released
+      mma_commit(drain_bar);
+      mbar_wait_drain(drain_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int i = warp >> 2;            // tile
+    const int row = (warp & 3) * 32 + lane;
+    const int mi = m0 + i * fwd::BM;
+    const int grow = mi + row;
+    const int nt = n_tiles[i];
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + i * 128;
+    const uint32_t t_o = tmem + lane_off + 256 + i * 128;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!(ok = mbar_wait(s_full(i), j & 1, abort_flag, kErrFwdSoftmax))) break;
+      tc_fence_after();
+      float s[fwd::BN];
+      {
+        uint32_t r[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]) * scale_log2;
+      }
+      const int n0 = j * fwd::BN;
+      const bool need_mask = (n0 + fwd::BN > S) || (CAUSAL && n0 + fwd::BN - 1 > mi);
+      if (need_mask) {
+        const int lim = CAUSAL ? min(S - 1, grow) : (S - 1);
+#pragma unroll
+        for (int c = 0; c < fwd::BN; ++c)
+          if (n0 + c > lim) s[c] = -INFINITY;
+      }
+      float tmax = s[0];
+#pragma unroll
+      for (int c = 1; c < fwd::BN; ++c) tmax = fmaxf(tmax, s[c]);
+      const float m_new = fmaxf(m_used, tmax);
+      const bool need = m_new > m_used + fwd::RESCALE_THRESHOLD;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_safe = (m_new == -INFINITY) ? 0.f : m_new;
+        const float alpha = fast_exp2(m_used - m_safe);
+        if (j > 0) {
+          // O_i(j-1) is complete: S_i(j) was committed after P_i(j-1) V_{j-1}.
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_o + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st32(t_o + c * 32, r);
+          }
+        }
+        l *= alpha;
+        m_used = m_new;
+      }
+      const float m_safe = (m_used == -INFINITY) ? 0.f : m_used;
+      uint32_t p[2][32];
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < fwd::BN / 2; ++c) {
+        const float p0 = fast_exp2(s[2 * c] - m_safe);
+        const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
+        rowsum += p0 + p1;
+        p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
+      }
+      l += rowsum;
+      tmem_st32(t_s, p[0]);
+      tmem_st32(t_s + 32, p[1]);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_ready(i));
+    }
+    if (ok && nt > 0) {
+      ok = mbar_wait(o_final(i), 0, abort_flag, kErrFwdSoftmax);
+      if (ok) {
+        tc_fence_after();
+        const float l_safe = (l == 0.f) ? 1.f : l;
+        const float inv_l = 1.f / l_safe;
+        __nv_bfloat16* orow = O + bh * o_stride_bh + static_cast<long long>(grow) * o_stride_s;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_o + c * 32, r);
+          tmem_ld_wait();
+          if (grow < S) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              packed[e] = pack_bf16x2(__uint_as_float(r[2 * e]) * inv_l, __uint_as_float(r[2 * e + 1]) * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              dst[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+          }
+        }
+        if (LSE != nullptr && grow < S) {
+          const float m_fin = (m_used == -INFINITY) ? 0.f : m_used;
+          LSE[static_cast<long long>(bh) * S + grow] = m_fin + __log2f(l_safe);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == fwd::MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// host launcher
+// ------------------------------------------------------------------------------------
+template <int D, bool CAUSAL>
+static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
+  using L = fwd::Layout<D>;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
+  if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
+  if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
+  auto kern = ffa_fwd_kernel<D, CAUSAL>;
+  static bool attr_set = false;  // per template instance
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+      return set_error(FFA_ERR_LAUNCH, "cudaFuncSetAttribute(fwd) failed");
+    attr_set = true;
+  }
+  const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
+  kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(a.o), a.lse,
+                                                        a.S, a.stride_bh, a.stride_s,
+                                                        static_cast<float>(a.scale * kLog2e));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
+  return FFA_OK;
+}
+
+int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
+  if (a.D == 128) return a.causal ? launch_fwd_t<128, true>(a, stream) : launch_fwd_t<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_fwd_t<64, true>(a, stream) : launch_fwd_t<64, false>(a, stream);
+  return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
+}
+
+}  // namespace ffa

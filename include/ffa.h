@@ -1,0 +1,79 @@
+/* ffa.h — C ABI of the B200 (sm_100a) exact bf16 attention library `libffa_sm100.so`.
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in elements) and a
+ * CUDA stream passed as `void*` (0 = legacy default stream).  No torch or C++ types cross
+ * this boundary.  Tensors are bf16 unless stated; logical layout is [BH, S, D] with the
+ * head dimension D contiguous (stride 1), rows `stride_s` elements apart and (batch*head)
+ * slices `stride_bh` elements apart.  Each call returns FFA_OK (0) or an FFA_ERR_* code;
+ * ffa_last_error() returns the message of the most recent failure on the calling thread.
+ *
+ * The kernels compute in bf16 with fp32 accumulation and handle D in {64, 128}
+ * natively; smaller power-of-two head dims are zero-padded to 64 by the Python layer
+ * (exact).  All kernels launch asynchronously on `stream`.
+ */
+#ifndef FFA_H_
+#define FFA_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFA_OK 0
+#define FFA_ERR_INVALID 1      /* bad pointer / size / stride / alignment */
+#define FFA_ERR_UNSUPPORTED 2  /* head_dim or shape outside what the kernels handle */
+#define FFA_ERR_LAUNCH 3       /* CUDA launch or driver error */
+#define FFA_ERR_DEVICE 4       /* a kernel recorded a device-side wait timeout */
+
+/* Forward.  Replaces the reference host launcher `fastflash_attn`
+ * (fastflash_attention/_kernel.py:282-318) and its kernel `_fastflash_fwd` (:180-279).
+ *   q, k, v  : [BH, S, D] bf16 inputs
+ *   o        : [BH, S, D] bf16 output (same strides as q)
+ *   lse      : [BH, S] fp32 base-2 log-sum-exp (m + log2 l), or NULL to skip it
+ *              (the reference's RETURN_LSE=False path, :303)
+ *   scale    : softmax scale; the kernel uses scale*log2(e) as the reference does (:304-305)
+ *   causal   : nonzero for top-left-aligned causal masking (key j visible iff j <= i) */
+int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH, int S, int D,
+            long long stride_bh, long long stride_s, double scale, int causal, void* stream);
+
+/* Backward preprocess: delta[bh, i] = sum_d O[bh,i,d] * dO[bh,i,d] in fp32.
+ * Replaces `_bwd_preprocess` / `_uni_bwd_preprocess` (_kernel.py:323-351). */
+int ffa_bwd_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D,
+                       long long stride_bh, long long stride_s, void* stream);
+
+/* Full deterministic backward: preprocess, then dK/dV (key-block grid) and dQ
+ * (query-block grid), each output tile written by exactly one CTA, no atomics.
+ * Replaces `FastFlashAttn.backward` (_kernel.py:784-906) with its kernels
+ * `_uni_bwd_dkdv` (:379-448) and `_uni_bwd_dq` (:487-564).
+ *   lse      : [BH, S] fp32 from ffa_fwd
+ *   delta_ws : [BH, S] fp32 caller-provided workspace (receives delta)
+ *   dq,dk,dv : [BH, S, D] bf16 outputs (same strides as q) */
+int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
+            float* delta_ws, void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh,
+            long long stride_s, double scale, int causal, void* stream);
+
+/* Merge of partial attention results for the context-parallel ring (no reference
+ * counterpart: the reference has no sequence parallelism; it builds on the base-2 LSE
+ * that `_fastflash_fwd` writes, _kernel.py:274-279).
+ *   acc [rows, D] fp32, acc_lse [rows] fp32 : running result (updated in place)
+ *   part [rows, D] bf16, part_lse [rows] fp32 : one partial result
+ * acc = (2^acc_lse * acc + 2^part_lse * part) / (2^acc_lse + 2^part_lse), acc_lse = log2 of the
+ * denominator.  `first` != 0 initialises acc from part. */
+int ffa_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,
+                  int first, void* stream);
+
+/* Most recent error message of the calling thread ("" if none). Copies at most n-1
+ * bytes into buf (NUL-terminated) and returns the last error code. */
+int ffa_last_error(char* buf, int n);
+
+/* Reads and clears the device status words of the current device:
+ * out[0] = id of the first wait that timed out (0 = none), out[1] = number of timed-out
+ * waits, out[2] = number of teardown drains that timed out.  Synchronises the device. */
+int ffa_device_status(unsigned int* out4);
+
+/* Library version string, e.g. "0.2.0+sm100a". */
+const char* ffa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FFA_H_ */
