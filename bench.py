@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path: causal D=128 forward + deterministic backward.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--S 8192]
+
+One step = one fused-attention forward plus the deterministic backward (autograd through
+``fastflashattention_b200.fast_attention``) over one batch of seeded N(0,1) bf16 inputs
+of the reference's headline shape B=4, H=16, S=8192, D=128, causal (
+the other configs are parity-test cases).  FLOPs follow the reference convention
+(bench/common.py:142-153): fwd = 4*B*H*S^2*D*(1/2 if causal), step = 3.5 * fwd.
+
+Multi-GPU (torchrun, one process per GPU): every rank owns a disjoint batch x head slice
+of a global batch of 4*N sequences (weak scaling, no data-path collective); the time is
+the max over ranks of the device-timed region.  Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's CPU path for this hot path — its parity
+oracle, fp32 ``F.scaled_dot_product_attention`` forward + autograd backward
+(oracle/sdpa_oracle.py) — on the host cores, one (batch, head) slice of the same
+workload per step, and prints the same JSON line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "fwd+bwd attention TFLOP/s (causal, D=128) and % of B200 bf16 tensor peak"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM bytes (read + write) per launch of the dK/dV kernel, from the ncu capture
+# summarised in profiles/bwd_dkdv_b1h16s8192d128_causal.md, scaled to the bench's
+# 64 (batch, head) slices.  None until a capture exists.
+DKDV_DRAM_BYTES_PER_SLICE = None
+
+
+def attn_flops(B, H, S, D, causal):
+    fwd = 4.0 * B * H * S * S * D * (0.5 if causal else 1.0)
+    return fwd, 3.5 * fwd
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons of one GPU while running."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        rows = []
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.bus_id and not parts[1].lower().endswith(self.bus_id[-12:]):
+                continue
+            rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
+        loaded = [x for x in sm if x > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[4]) for r in rows
+                                                         if r[4].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------------- CPU oracle
+def cpu_reference_sample(S, D, causal, heads=1, reps=1, seed=0):
+    """fp32 math-SDPA forward+backward on the host (the reference's parity oracle) for
+    `heads` (batch, head) slices of length S.  Returns (seconds per slice, threads)."""
+    import torch
+    sys.path.insert(0, str(ROOT))
+    from oracle.sdpa_oracle import sdpa_fwd_bwd
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda: torch.randn(1, heads, S, D, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, k, v, do = mk(), mk(), mk(), mk()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        sdpa_fwd_bwd(q, k, v, do, causal)
+        times.append(time.perf_counter() - t0)
+    return min(times) / heads, threads
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    B, H, S, D, causal = args.B, args.H, args.S, args.D, True
+    _, step_flops_slice = attn_flops(1, 1, S, D, causal)
+    secs = []
+    threads = 1
+    for i in range(args.warmup + args.steps):
+        s, threads = cpu_reference_sample(S, D, causal, heads=1, reps=1, seed=i)
+        if i >= args.warmup:
+            secs.append(s)
+    t = statistics.median(secs)
+    value = step_flops_slice / t / 1e12
+    sample = f"one (batch, head) slice of B{B} H{H} S{S} D{D} causal per step (1/{B * H} of the workload)"
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1e3 * B * H, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) bf16 inputs, seeded",
+        "impl": "reference",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "fp32 F.scaled_dot_product_attention (math) fwd + autograd bwd on host cores: the reference's "
+                "parity oracle (tests/test_parity.py:32-35); ms_per_step extrapolated to the full batch",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, world):
+    return {
+        "workload": f"B{args.B} H{args.H} S{args.S} D{args.D} causal fwd+bwd per GPU (weak scaling: global B={args.B * world})",
+        "B": args.B, "H": args.H, "S": args.S, "D": args.D, "causal": True,
+        "global_batch": args.B * world, "seq_len": args.S,
+        "parallelism": f"dp{world} (disjoint batch x head slices, no collective)",
+        "l2": "inputs larger than L2: q, k, v, dO are 4 x %d MiB per GPU" % (args.B * args.H * args.S * args.D * 2 >> 20),
+    }
+
+
+# ------------------------------------------------------------------------------ ours
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, str(ROOT))
+    from fastflashattention_b200 import _lib, fast_attention
+    from fastflashattention_b200._kernel import fastflash_attn
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, H, S, D = args.B, args.H, args.S, args.D
+    causal = True
+    fwd_flops, step_flops = attn_flops(B, H, S, D, causal)
+    gen = torch.Generator(device=dev).manual_seed(1000 * rank)
+    mk = lambda: torch.randn(B, H, S, D, device=dev, dtype=torch.bfloat16, generator=gen)  # noqa: E731
+    q, k, v, do = mk(), mk(), mk(), mk()
+    qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+
+    def step():
+        o = fast_attention(qg, kg, vg, is_causal=causal)
+        return torch.autograd.grad(o, (qg, kg, vg), do)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    props = torch.cuda.get_device_properties(dev)
+    bus = getattr(props, "pci_bus_id", None)
+    if bus is None:
+        try:
+            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+        except AttributeError:
+            bus = None
+    sampler = ClockSampler(str(bus) if bus is not None else None)
+    sampler.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * step_flops / (ms / 1e3) / 1e12
+
+    # ---- per-kernel times (same inputs, each kernel alone, CUDA events on this stream)
+    lib = _lib.load()
+    BH = B * H
+    qf, kf, vf, dof = (t.reshape(BH, S, D) for t in (q, k, v, do))
+    o, lse = fastflash_attn(q, k, v, causal, return_lse=True)
+    of, lf = o.reshape(BH, S, D), lse.reshape(BH, S)
+    delta = torch.empty(BH, S, device=dev, dtype=torch.float32)
+    dq, dk, dv = (torch.empty_like(qf) for _ in range(3))
+    sm = 1.0 / math.sqrt(D)
+    sp = stream.cuda_stream
+    st = D * 1, S * D
+    kernels = {
+        "fwd": lambda: lib.ffa_fwd(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), of.data_ptr(), lf.data_ptr(),
+                                   BH, S, D, st[1], st[0], sm, 1, sp),
+        "bwd_preprocess": lambda: lib.ffa_bwd_preprocess(of.data_ptr(), dof.data_ptr(), delta.data_ptr(), BH, S, D,
+                                                         st[1], st[0], sp),
+        "bwd_dkdv": lambda: lib.ffa_bwd_dkdv(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), dof.data_ptr(),
+                                             lf.data_ptr(), delta.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                             BH, S, D, st[1], st[0], sm, 1, sp),
+        "bwd_dq": lambda: lib.ffa_bwd_dq(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), dof.data_ptr(), lf.data_ptr(),
+                                         delta.data_ptr(), dq.data_ptr(), BH, S, D, st[1], st[0], sm, 1, sp),
+    }
+    half = 0.5
+    mm = 2.0 * BH * S * S * D * half  # one S x S x D contraction, causal half
+    algo = {"fwd": (2 * mm, "flop"), "bwd_dkdv": (4 * mm, "flop"), "bwd_dq": (3 * mm, "flop"),
+            "bwd_preprocess": (2.0 * BH * S * D * 2 + BH * S * 4, "byte")}
+    kinfo = {}
+    for name, fn in kernels.items():
+        for _ in range(3):
+            _lib.check(fn(), name)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(3, args.steps)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        kms = a.elapsed_time(b) / n
+        amount, kind = algo[name]
+        rate = amount / (kms / 1e3) / (1e12 if kind == "flop" else 1e9)
+        kinfo[name] = {"ms": round(kms, 4), ("tflops" if kind == "flop" else "gbs"): round(rate, 1)}
+    status = _lib.device_status()
+
+    peaks, peak_kind = load_peaks()
+    dk_ms = kinfo["bwd_dkdv"]["ms"]
+    achieved = algo["bwd_dkdv"][0] / (dk_ms / 1e3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    traffic = None if DKDV_DRAM_BYTES_PER_SLICE is None else DKDV_DRAM_BYTES_PER_SLICE * BH
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": "ffa_bwd_dkdv_kernel",
+                "peak_source": f"{peak_kind} bf16_tflops (burst; the kernel is timed alone)",
+                "algorithmic": "4 contractions (S^T, dP^T, dV, dK) x 2*B*H*S^2*D x 1/2 causal per launch"}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+        gq, gk, gv = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, k, v))
+        dq_in, dk_in, dv_in, ddo = (torch.empty_like(q) for _ in range(4))
+
+        def e2e_step():
+            with torch.no_grad():
+                dq_in.copy_(hq, non_blocking=True)
+                dk_in.copy_(hk, non_blocking=True)
+                dv_in.copy_(hv, non_blocking=True)
+                ddo.copy_(hdo, non_blocking=True)
+            a_, b_, c_ = (t.detach().requires_grad_(True) for t in (dq_in, dk_in, dv_in))
+            o_ = fast_attention(a_, b_, c_, is_causal=causal)
+            g = torch.autograd.grad(o_, (a_, b_, c_), ddo)
+            gq.copy_(g[0], non_blocking=True)
+            gk.copy_(g[1], non_blocking=True)
+            gv.copy_(g[2], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ems], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        nbytes = q.numel() * q.element_size()
+        e2e = {"value": world * step_flops / (ems / 1e3) / 1e12, "unit": UNIT, "ms_per_step": ems,
+               "h2d_bytes_per_step": 4 * nbytes * world, "d2h_bytes_per_step": 3 * nbytes * world,
+               "path": "pinned host q,k,v,dO -> fast_attention fwd + autograd bwd -> dq,dk,dv to pinned host"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        secs, threads = cpu_reference_sample(S, D, causal, heads=1, reps=2)
+        _, flops_slice = attn_flops(1, 1, S, D, causal)
+        cpu = {"value": flops_slice / secs / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"one (batch, head) slice of B{B} H{H} S{S} D{D} causal, fp32 math SDPA fwd+bwd, best of 2",
+               "ms_per_slice": secs * 1e3}
+
+    if rank == 0:
+        spec = 2250.0
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1) bf16 inputs, seeded (no dataset)",
+            "config": config_dict(args, world),
+            "pct_peak": {"of_measured_bf16": round(100 * value / world / peak, 2),
+                         "of_spec_2250": round(100 * value / world / spec, 2)},
+            "roofline": roofline,
+            "kernels": kinfo,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": 4 * args.steps,
+            "device_status": list(status),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--B", type=int, default=4)
+    ap.add_argument("--H", type=int, default=16)
+    ap.add_argument("--S", type=int, default=8192)
+    ap.add_argument("--D", type=int, default=128)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -113,9 +113,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nblk = gridDim.x;
-  const int kblk = static_cast<int>(blockIdx.x);  // causal: low key blocks carry the most work, run them first
-  (void)nblk;
+  const int kblk = static_cast<int>(blockIdx.x);  // causal: low key blocks carry the most work and run first
   const int bh = blockIdx.y;
   const int n0 = kblk * bwd::LANES;
   const int q_begin = CAUSAL ? n0 : 0;  // first query that can see a key of this block
@@ -262,7 +260,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       const float* lse_s = reinterpret_cast<const float*>(stage_ptr(s) + 2 * L::STEP_TILE) + 32 * g;
       const float* dl_s = lse_s + bwd::STEP;
       const int qc = q_begin + i * bwd::STEP + 32 * g;  // first query of this thread's columns
-      const bool need_mask = CAUSAL && (qc < kg + 1 + 31) && (qc <= n0 + bwd::LANES - 1);
+      const bool need_mask = CAUSAL && (qc < kg);  // some query of these columns precedes the key
       uint32_t pp[16], dsp[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
@@ -533,52 +531,70 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------
-// host launcher
+// host launchers
 // ------------------------------------------------------------------------------------
 template <int D, bool CAUSAL>
-static int launch_bwd_t(const BwdArgs& a, cudaStream_t stream) {
+static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   using LK = bwd::DkdvLayout<D>;
-  using LQ = bwd::DqLayout<D>;
-  CUtensorMap tq128, tdo128, tk64, tv64, tk128, tv128, tq64, tdo64;
+  CUtensorMap tk, tv, tq, tdo;
   int rc;
-  if ((rc = make_tile_map(&tq128, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tdo128, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tk128, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tv128, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tq64, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, 64))) return rc;
-  if ((rc = make_tile_map(&tdo64, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 64))) return rc;
-  if ((rc = make_tile_map(&tk64, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, 64))) return rc;
-  if ((rc = make_tile_map(&tv64, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 64))) return rc;
-  auto kdkdv = ffa_bwd_dkdv_kernel<D, CAUSAL>;
-  auto kdq = ffa_bwd_dq_kernel<D, CAUSAL>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, LK::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, LQ::SMEM_BYTES) != cudaSuccess)
-      return set_error(FFA_ERR_LAUNCH, "cudaFuncSetAttribute(bwd) failed");
-    attr_set = true;
-  }
-  if ((rc = launch_preprocess(a.o, a.dout, a.delta, a.BH, a.S, D, a.stride_bh, a.stride_s, stream))) return rc;
-  const float scale = static_cast<float>(a.scale);
-  const float scale_log2 = static_cast<float>(a.scale * kLog2e);
+  if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::LANES))) return rc;
+  if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::LANES))) return rc;
+  if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::STEP))) return rc;
+  if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::STEP))) return rc;
+  auto kern = ffa_bwd_dkdv_kernel<D, CAUSAL>;
+  static unsigned long long configured = 0;
+  if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LK::SMEM_BYTES, &configured))) return rc;
   const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
-  kdkdv<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(
-      tk128, tv128, tq64, tdo64, a.lse, a.delta, static_cast<__nv_bfloat16*>(a.dk), static_cast<__nv_bfloat16*>(a.dv),
-      a.S, a.stride_bh, a.stride_s, scale_log2, scale);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
-  kdq<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq128, tdo128, tk64, tv64, a.lse, a.delta,
-                                                       static_cast<__nv_bfloat16*>(a.dq), a.S, a.stride_bh,
-                                                       a.stride_s, scale_log2, scale);
-  e = cudaGetLastError();
+  kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, a.lse, a.delta,
+                                                        static_cast<__nv_bfloat16*>(a.dk),
+                                                        static_cast<__nv_bfloat16*>(a.dv), a.S, a.stride_bh,
+                                                        a.stride_s, static_cast<float>(a.scale * kLog2e),
+                                                        static_cast<float>(a.scale));
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
   return FFA_OK;
 }
 
-int launch_bwd(const BwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_bwd_t<128, true>(a, stream) : launch_bwd_t<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_bwd_t<64, true>(a, stream) : launch_bwd_t<64, false>(a, stream);
+template <int D, bool CAUSAL>
+static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
+  using LQ = bwd::DqLayout<D>;
+  CUtensorMap tq, tdo, tk, tv;
+  int rc;
+  if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::LANES))) return rc;
+  if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::LANES))) return rc;
+  if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::STEP))) return rc;
+  if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, bwd::STEP))) return rc;
+  auto kern = ffa_bwd_dq_kernel<D, CAUSAL>;
+  static unsigned long long configured = 0;
+  if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
+  const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
+  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, a.lse, a.delta,
+                                                        static_cast<__nv_bfloat16*>(a.dq), a.S, a.stride_bh,
+                                                        a.stride_s, static_cast<float>(a.scale * kLog2e),
+                                                        static_cast<float>(a.scale));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
+  return FFA_OK;
+}
+
+int launch_dkdv(const BwdArgs& a, cudaStream_t stream) {
+  if (a.D == 128) return a.causal ? launch_dkdv_t<128, true>(a, stream) : launch_dkdv_t<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_dkdv_t<64, true>(a, stream) : launch_dkdv_t<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
+}
+
+int launch_dq(const BwdArgs& a, cudaStream_t stream) {
+  if (a.D == 128) return a.causal ? launch_dq_t<128, true>(a, stream) : launch_dq_t<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_dq_t<64, true>(a, stream) : launch_dq_t<64, false>(a, stream);
+  return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
+}
+
+int launch_bwd(const BwdArgs& a, cudaStream_t stream) {
+  int rc;
+  if ((rc = launch_preprocess(a.o, a.dout, a.delta, a.BH, a.S, a.D, a.stride_bh, a.stride_s, stream))) return rc;
+  if ((rc = launch_dkdv(a, stream))) return rc;
+  return launch_dq(a, stream);
 }
 
 }  // namespace ffa

@@ -45,6 +45,16 @@ int set_error(int code, const char* msg) {
   return code;
 }
 
+// Make the current device's primary context current on the calling thread.  Callers
+// such as torch's autograd worker threads select a device without ever touching the
+// runtime, and the driver-level tensor-map encoder needs a current context.
+int ensure_context() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "no usable CUDA device on this thread");
+  return FFA_OK;
+}
+
 int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,
                   long long stride_s, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
@@ -61,6 +71,17 @@ int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long
     std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
     return set_error(FFA_ERR_INVALID, buf);
   }
+  return FFA_OK;
+}
+
+int set_smem_once(const void* kernel, int bytes, unsigned long long* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaGetDevice failed");
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (__atomic_load_n(done, __ATOMIC_ACQUIRE) & bit) return FFA_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
+  __atomic_fetch_or(done, bit, __ATOMIC_ACQ_REL);
   return FFA_OK;
 }
 
@@ -88,6 +109,7 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
   if (!q || !k || !v || !o) return set_error(FFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
   FwdArgs a{q, k, v, o, lse, BH, S, D, stride_bh, stride_s, scale, causal};
   return launch_fwd(a, static_cast<cudaStream_t>(stream));
 }
@@ -99,6 +121,7 @@ int ffa_bwd_preprocess(const void* o, const void* dout, float* delta, int BH, in
   if (BH == 0 || S == 0) return FFA_OK;
   if (!o || !dout || !delta) return set_error(FFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(o) || !aligned16(dout)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
   return launch_preprocess(o, dout, delta, BH, S, D, stride_bh, stride_s, static_cast<cudaStream_t>(stream));
 }
 
@@ -113,8 +136,40 @@ int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const vo
   for (const void* p : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
                         static_cast<const void*>(dv)})
     if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
   BwdArgs a{q, k, v, o, dout, lse, delta_ws, dq, dk, dv, BH, S, D, stride_bh, stride_s, scale, causal};
   return launch_bwd(a, static_cast<cudaStream_t>(stream));
+}
+
+// Shared validation of the split backward entry points (lse and delta are inputs).
+static int bwd_part(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                    const float* delta, void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh,
+                    long long stride_s, double scale, int causal, void* stream, bool dkdv) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !dout || !lse || !delta || (dkdv ? (!dk || !dv) : !dq))
+    return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  for (const void* p : {q, k, v, dout, static_cast<const void*>(dkdv ? dk : dq), static_cast<const void*>(dkdv ? dv : dq)})
+    if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
+  BwdArgs a{q, k, v, nullptr, dout, lse, const_cast<float*>(delta), dq, dk, dv, BH, S, D, stride_bh, stride_s, scale,
+            causal};
+  return dkdv ? launch_dkdv(a, static_cast<cudaStream_t>(stream)) : launch_dq(a, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+                 void* dk, void* dv, int BH, int S, int D, long long stride_bh, long long stride_s, double scale,
+                 int causal, void* stream) {
+  return bwd_part(q, k, v, dout, lse, delta, nullptr, dk, dv, BH, S, D, stride_bh, stride_s, scale, causal, stream,
+                  true);
+}
+
+int ffa_bwd_dq(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+               void* dq, int BH, int S, int D, long long stride_bh, long long stride_s, double scale, int causal,
+               void* stream) {
+  return bwd_part(q, k, v, dout, lse, delta, dq, nullptr, nullptr, BH, S, D, stride_bh, stride_s, scale, causal,
+                  stream, false);
 }
 
 int ffa_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,
@@ -124,6 +179,8 @@ int ffa_lse_merge(float* acc, float* acc_lse, const void* part, const float* par
   if (!acc || !acc_lse || !part || !part_lse) return set_error(FFA_ERR_INVALID, "null tensor pointer");
   if (!aligned16(acc) || (reinterpret_cast<uintptr_t>(part) & 7u))
     return set_error(FFA_ERR_INVALID, "acc must be 16-byte and part 8-byte aligned");
+  const int rc = ensure_context();
+  if (rc != FFA_OK) return rc;
   return launch_lse_merge(acc, acc_lse, part, part_lse, rows, D, first, static_cast<cudaStream_t>(stream));
 }
 

@@ -57,6 +57,10 @@ struct BwdArgs {
 
 // host helpers (ffa_capi.cu)
 int set_error(int code, const char* msg);
+int ensure_context();
+// Raise a kernel's dynamic shared-memory limit once per device; `done` is a per-kernel
+// bitmask of devices already configured.
+int set_smem_once(const void* kernel, int bytes, unsigned long long* done);
 // 3-D tensor map over a [BH, S, D] bf16 tensor: box = 64 columns x `box_rows` rows x 1
 // slice, 128-byte swizzle (the layout the tcgen05 descriptors in sm100.cuh expect).
 int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,
@@ -64,6 +68,8 @@ int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream);
 int launch_bwd(const BwdArgs& a, cudaStream_t stream);
+int launch_dkdv(const BwdArgs& a, cudaStream_t stream);
+int launch_dq(const BwdArgs& a, cudaStream_t stream);
 int launch_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D, long long stride_bh,
                       long long stride_s, cudaStream_t stream);
 int launch_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,

@@ -355,12 +355,8 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   auto kern = ffa_fwd_kernel<D, CAUSAL>;
-  static bool attr_set = false;  // per template instance
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
-      return set_error(FFA_ERR_LAUNCH, "cudaFuncSetAttribute(fwd) failed");
-    attr_set = true;
-  }
+  static unsigned long long configured = 0;  // devices with the smem limit raised
+  if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
   kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(a.o), a.lse,
                                                         a.S, a.stride_bh, a.stride_s,

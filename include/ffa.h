@@ -51,6 +51,18 @@ int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const vo
             float* delta_ws, void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh,
             long long stride_s, double scale, int causal, void* stream);
 
+/* The two gradient kernels of ffa_bwd, callable on their own (delta from
+ * ffa_bwd_preprocess).  ffa_bwd_dkdv replaces `_bwd_dkdv` (_kernel.py:451-484, kernel
+ * :379-448): grid over 128-key blocks, writes dk, dv.  ffa_bwd_dq replaces `_bwd_dq`
+ * (_kernel.py:567-602, kernel :487-564, recompute path): grid over 128-query blocks,
+ * writes dq.  Each output tile is written by exactly one CTA. */
+int ffa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+                 void* dk, void* dv, int BH, int S, int D, long long stride_bh, long long stride_s, double scale,
+                 int causal, void* stream);
+int ffa_bwd_dq(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+               void* dq, int BH, int S, int D, long long stride_bh, long long stride_s, double scale, int causal,
+               void* stream);
+
 /* Merge of partial attention results for the context-parallel ring (no reference
  * counterpart: the reference has no sequence parallelism; it builds on the base-2 LSE
  * that `_fastflash_fwd` writes, _kernel.py:274-279).
