@@ -37,9 +37,9 @@ UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per launch of the dK/dV kernel, from the ncu capture
-# summarised in profiles/bwd_dkdv_b1h16s8192d128_causal.md, scaled to the bench's
-# 64 (batch, head) slices.  None until a capture exists.
-DKDV_DRAM_BYTES_PER_SLICE = None
+# summarised in profiles/bwd_dkdv_b2h16s8192d128_causal.md (B2 H16 = 32 slices), scaled to the
+# bench's (batch, head) slice count.
+DKDV_DRAM_BYTES_PER_SLICE = (270.6432e6 + 106.433536e6) / 32
 
 
 def attn_flops(B, H, S, D, causal):
@@ -63,8 +63,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, bus_id: str | None):
+    def __init__(self, bus_id: str | None, fallback_index: int = 0):
         self.bus_id = (bus_id or "").lower()
+        self.fallback_index = str(fallback_index)
         self.proc = None
         self.lines: list[str] = []
         self._t = None
@@ -94,14 +95,10 @@ class ClockSampler:
             self.proc.kill()
         if self._t:
             self._t.join(timeout=2)
-        rows = []
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 10:
-                continue
-            if self.bus_id and not parts[1].lower().endswith(self.bus_id[-12:]):
-                continue
-            rows.append(parts)
+        allrows = [p for p in ([x.strip() for x in ln.split(",")] for ln in self.lines) if len(p) >= 10]
+        rows = [p for p in allrows if self.bus_id and p[1].lower().endswith(self.bus_id[-7:])]
+        if not rows:  # bus id unknown or not matched: nvidia-smi index of the local device
+            rows = [p for p in allrows if p[0] == self.fallback_index]
         if not rows:
             return None
         sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
@@ -112,6 +109,15 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
                 "samples": len(rows), "power_w_max": max(float(r[4]) for r in rows
                                                          if r[4].replace(".", "").isdigit())}
+
+
+def pci_bus_string(props):
+    """nvidia-smi style bus id ("00000000:1B:00.0") of a torch device, or None."""
+    try:
+        dom, bus, devn = int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id)
+    except (AttributeError, TypeError, ValueError):
+        return None
+    return "%08X:%02X:%02X.0" % (dom, bus, devn)
 
 
 # ------------------------------------------------------------------------- CPU oracle
@@ -203,14 +209,7 @@ def run_ours(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize()
 
-    props = torch.cuda.get_device_properties(dev)
-    bus = getattr(props, "pci_bus_id", None)
-    if bus is None:
-        try:
-            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
-        except AttributeError:
-            bus = None
-    sampler = ClockSampler(str(bus) if bus is not None else None)
+    sampler = ClockSampler(pci_bus_string(torch.cuda.get_device_properties(dev)), local_rank)
     sampler.start()
     time.sleep(0.3)
     stream = torch.cuda.current_stream(dev)
