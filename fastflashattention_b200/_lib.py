@@ -27,6 +27,7 @@ SIGNATURES = {
     "ffa_fwd": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_preprocess": (_I, [_VP, _VP, _VP, _I, _I, _I, _LL, _LL, _VP]),
     "ffa_bwd": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
+    "ffa_bwd_noalloc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_dkdv": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_dq": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_lse_merge": (_I, [_VP, _VP, _VP, _VP, _LL, _I, _I, _VP]),

@@ -85,6 +85,43 @@ int set_smem_once(const void* kernel, int bytes, unsigned long long* done) {
   return FFA_OK;
 }
 
+// ------------------------------------------------------------------------------------
+// Fixed scratch of ffa_bwd_noalloc.  The backward needs one fp32 per (slice, row) for
+// delta = rowsum(O * dO).  Callers that cannot allocate device memory get it from this
+// file-scope array instead; it is part of the library image, so every GPU that loads
+// the library holds its 16 MiB until the process exits.  Host code must not use the
+// array's name as a device address: the device address is looked up per device with
+// cudaGetSymbolAddress (noalloc_delta_ptr below).
+// ------------------------------------------------------------------------------------
+constexpr long long kNoAllocDeltaRows = 4ll << 20;  // 4,194,304 rows = 16 MiB of fp32
+static __device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaRows];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_delta_dev[64] = {};  // device address of g_noalloc_delta, per device ordinal
+}  // namespace
+
+// Device address of g_noalloc_delta on the current device, looked up on the first call
+// for that device (which therefore must not happen inside a stream capture).
+static int noalloc_delta_ptr(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaGetDevice failed");
+  if (dev < 0 || dev >= 64) return set_error(FFA_ERR_UNSUPPORTED, "device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_delta_dev[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_delta);
+    if (e != cudaSuccess || p == nullptr) {
+      char buf[160];
+      std::snprintf(buf, sizeof(buf), "cudaGetSymbolAddress(no-alloc scratch) failed: %s", cudaGetErrorString(e));
+      return set_error(FFA_ERR_LAUNCH, buf);
+    }
+    g_noalloc_delta_dev[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_delta_dev[dev];
+  return FFA_OK;
+}
+
 // Shape / stride / alignment checks shared by the entry points.
 static int check_common(int BH, int S, int D, long long stride_bh, long long stride_s) {
   if (BH < 0 || S < 0) return set_error(FFA_ERR_INVALID, "BH and S must be non-negative");
@@ -138,6 +175,30 @@ int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const vo
     if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
   if ((rc = ensure_context()) != FFA_OK) return rc;
   BwdArgs a{q, k, v, o, dout, lse, delta_ws, dq, dk, dv, BH, S, D, stride_bh, stride_s, scale, causal};
+  return launch_bwd(a, static_cast<cudaStream_t>(stream));
+}
+
+// Same backward as ffa_bwd, with delta kept in the library's fixed device scratch
+// instead of a caller-provided buffer; it allocates nothing.  Calls that overlap on the
+// GPU (other streams, other threads) share that scratch and race; serialise them.
+int ffa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
+                    void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh, long long stride_s,
+                    double scale, int causal, void* stream) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (static_cast<long long>(BH) * S > kNoAllocDeltaRows)
+    return set_error(FFA_ERR_INVALID, "ffa_bwd_noalloc: BH*S exceeds its fixed scratch of 4194304 rows");
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv)
+    return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  for (const void* p : {q, k, v, o, dout, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                        static_cast<const void*>(dv)})
+    if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
+  float* delta = nullptr;
+  if ((rc = noalloc_delta_ptr(&delta)) != FFA_OK) return rc;
+  // delta is fully rewritten by the preprocess kernel before it is read: nothing to clear
+  BwdArgs a{q, k, v, o, dout, lse, delta, dq, dk, dv, BH, S, D, stride_bh, stride_s, scale, causal};
   return launch_bwd(a, static_cast<cudaStream_t>(stream));
 }
 

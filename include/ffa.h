@@ -51,6 +51,21 @@ int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const vo
             float* delta_ws, void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh,
             long long stride_s, double scale, int causal, void* stream);
 
+/* ffa_bwd without any device allocation, for callers that cannot call cudaMalloc:
+ * a framework whose allocator owns nearly all device memory (XLA/TensorFlow-style
+ * preallocation, serving runtimes with a fixed memory pool), or code running where
+ * allocating is not allowed.  No counterpart in the reference (its backward always
+ * allocates through the torch caching allocator).
+ * The caller still passes inputs and outputs; the fp32 delta workspace lives in a
+ * fixed 16 MiB array inside the library (held on every GPU that loads the library
+ * until the process exits), so BH*S must be <= 4194304 (else FFA_ERR_INVALID).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * All calls share the one array: calls that overlap on the GPU race — serialise them. */
+int ffa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
+                    void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh, long long stride_s,
+                    double scale, int causal, void* stream);
+
 /* The two gradient kernels of ffa_bwd, callable on their own (delta from
  * ffa_bwd_preprocess).  ffa_bwd_dkdv replaces `_bwd_dkdv` (_kernel.py:451-484, kernel
  * :379-448): grid over 128-key blocks, writes dk, dv.  ffa_bwd_dq replaces `_bwd_dq`
