@@ -54,13 +54,16 @@ struct DkdvLayout {
 template <int D>
 struct DqLayout {
   static constexpr int TILE = 128 * D * 2;  // Q, dO (resident) and K, V (streamed) tiles
+  static constexpr int K_STAGES = 3;        // K_j is read by S_j and, a step later, by dQ += dS_j K_j
+  static constexpr int V_STAGES = 2;        // V_j is read by dP_j only
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;
-  static constexpr int STAGE_BYTES = 2 * TILE;  // K tile, V tile
-  static constexpr int BAR_OFF = STAGE_OFF + STAGES * STAGE_BYTES;
-  // qd_full, kv_full[2], kv_empty[2], s_full[2], dp_full, dp_free, ds_ready, final, drain
-  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 5;
+  static constexpr int K_OFF = 2 * TILE;
+  static constexpr int V_OFF = K_OFF + K_STAGES * TILE;
+  static constexpr int BAR_OFF = V_OFF + V_STAGES * TILE;
+  // qd_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], dp_full, dp_free,
+  // ds_ready, final, drain
+  static constexpr int NBARS = 1 + 2 * K_STAGES + 2 * V_STAGES + 2 + 5;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
 };
@@ -369,11 +372,14 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::BAR_OFF;
+  constexpr int KS = L::K_STAGES, VS = L::V_STAGES;
   const uint32_t qd_full = bar0;
-  auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8 * (1 + bwd::STAGES + s); };
-  auto s_full = [&](int b) { return bar0 + 8 * (1 + 2 * bwd::STAGES + b); };
-  const uint32_t dp_full = bar0 + 8 * (3 + 2 * bwd::STAGES);
+  auto k_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8 * (1 + KS + s); };
+  auto v_full = [&](int s) { return bar0 + 8 * (1 + 2 * KS + s); };
+  auto v_empty = [&](int s) { return bar0 + 8 * (1 + 2 * KS + VS + s); };
+  auto s_full = [&](int b) { return bar0 + 8 * (1 + 2 * KS + 2 * VS + b); };
+  const uint32_t dp_full = bar0 + 8 * (3 + 2 * KS + 2 * VS);
   const uint32_t dp_free = dp_full + 8;
   const uint32_t ds_ready = dp_full + 16;
   const uint32_t final_bar = dp_full + 24;
@@ -392,9 +398,13 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(qd_full, 1);
-    for (int s = 0; s < bwd::STAGES; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
     }
     mbar_init(s_full(0), 1);
     mbar_init(s_full(1), 1);
@@ -430,22 +440,26 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         tma_load_3d(sbase + L::Q_OFF + sl * 16384, &tm_q, qd_full, sl * 64, m0, bh, keep);
         tma_load_3d(sbase + L::DO_OFF + sl * 16384, &tm_do, qd_full, sl * 64, m0, bh, keep);
       }
-      int issued = 0;
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < nk; ++j) {
-        const int s = j % bwd::STAGES;
-        if (!mbar_wait(kv_empty(s), ((j / bwd::STAGES) & 1) ^ 1, abort_flag, kErrDqProducer)) break;
-        const uint32_t st = sbase + L::STAGE_OFF + s * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(kv_full(s), 2 * L::TILE);
-        for (int sl = 0; sl < SLABS; ++sl) {
-          tma_load_3d(st + sl * 16384, &tm_k, kv_full(s), sl * 64, j * bwd::STEP, bh, keep);
-          tma_load_3d(st + L::TILE + sl * 16384, &tm_v, kv_full(s), sl * 64, j * bwd::STEP, bh, keep);
-        }
-        ++issued;
+        const int sk = j % KS, sv = j % VS;
+        if (!mbar_wait(k_empty(sk), ((j / KS) & 1) ^ 1, abort_flag, kErrDqProducer)) break;
+        mbar_arrive_expect_tx(k_full(sk), L::TILE);
+        for (int sl = 0; sl < SLABS; ++sl)
+          tma_load_3d(sbase + L::K_OFF + sk * L::TILE + sl * 16384, &tm_k, k_full(sk), sl * 64, j * bwd::STEP, bh,
+                      keep);
+        ++k_issued;
+        if (!mbar_wait(v_empty(sv), ((j / VS) & 1) ^ 1, abort_flag, kErrDqProducer)) break;
+        mbar_arrive_expect_tx(v_full(sv), L::TILE);
+        for (int sl = 0; sl < SLABS; ++sl)
+          tma_load_3d(sbase + L::V_OFF + sv * L::TILE + sl * 16384, &tm_v, v_full(sv), sl * 64, j * bwd::STEP, bh,
+                      keep);
+        ++v_issued;
       }
       if (*abort_flag) {
         mbar_wait_drain(qd_full, 0);
-        for (int it = max(0, issued - bwd::STAGES); it < issued; ++it)
-          mbar_wait_drain(kv_full(it % bwd::STAGES), (it / bwd::STAGES) & 1);
+        for (int it = max(0, k_issued - KS); it < k_issued; ++it) mbar_wait_drain(k_full(it % KS), (it / KS) & 1);
+        for (int it = max(0, v_issued - VS); it < v_issued; ++it) mbar_wait_drain(v_full(it % VS), (it / VS) & 1);
       }
     }
   } else if (warp == bwd::MMA_WARP) {
@@ -454,9 +468,10 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       constexpr uint32_t IDESC_SD = idesc_bf16(128, bwd::STEP, false, false);  // [128 queries x 128 keys]
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);            // [128 queries x D]
       const uint32_t q_addr = sbase + L::Q_OFF, do_addr = sbase + L::DO_OFF;
-      auto k_addr = [&](int j) { return sbase + L::STAGE_OFF + (j % bwd::STAGES) * L::STAGE_BYTES; };
+      auto k_addr = [&](int j) { return sbase + L::K_OFF + (j % KS) * L::TILE; };
+      auto v_addr = [&](int j) { return sbase + L::V_OFF + (j % VS) * L::TILE; };
       auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into buffer j&1
-        if (!mbar_wait(kv_full(j % bwd::STAGES), (j / bwd::STAGES) & 1, abort_flag, kErrDqMma)) return false;
+        if (!mbar_wait(k_full(j % KS), (j / KS) & 1, abort_flag, kErrDqMma)) return false;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
@@ -465,12 +480,15 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         mma_commit(s_full(j & 1));
         return true;
       };
-      auto issue_dp = [&](int j) {  // dP_j = dO V_j^T
+      auto issue_dp = [&](int j) -> bool {  // dP_j = dO V_j^T
+        if (!mbar_wait(v_full(j % VS), (j / VS) & 1, abort_flag, kErrDqMma)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tmem + 128, kmajor_desc(do_addr, 128, ks), kmajor_desc(k_addr(j) + L::TILE, 128, ks), IDESC_SD,
-                 ks > 0);
+          mma_ss(tmem + 128, kmajor_desc(do_addr, 128, ks), kmajor_desc(v_addr(j), 128, ks), IDESC_SD, ks > 0);
         mma_commit(dp_full);
+        mma_commit(v_empty(j % VS));
+        return true;
       };
       auto issue_g = [&](int j) -> bool {  // dQ += dS_j K_j
         if (!mbar_wait(ds_ready, j & 1, abort_flag, kErrDqMma)) return false;
@@ -479,13 +497,13 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         for (int ks = 0; ks < bwd::STEP / 16; ++ks)
           mma_ts(tmem + 256, bwd::packed_kstep_col(tmem + dq_sbuf(j & 1), ks), mnmajor_desc(k_addr(j), 128, ks),
                  IDESC_G, (j > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(kv_empty(j % bwd::STAGES));
+        mma_commit(k_empty(j % KS));
         return true;
       };
       bool ok = mbar_wait(qd_full, 0, abort_flag, kErrDqMma);
       if (ok && nk > 0) {
         ok = issue_s(0);
-        if (ok) issue_dp(0);
+        if (ok) ok = issue_dp(0);
       }
       // S(j+1) and dP(j+1) run while the warpgroups turn step j into dS; dP(j+1) waits
       // only until the warpgroups have copied dP(j) out of tensor memory.
@@ -494,7 +512,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           if (!(ok = issue_s(j + 1))) break;
           if (!(ok = mbar_wait(dp_free, j & 1, abort_flag, kErrDqMma))) break;
           tc_fence_after();
-          issue_dp(j + 1);
+          if (!(ok = issue_dp(j + 1))) break;
         }
         if (!(ok = issue_g(j))) break;
       }

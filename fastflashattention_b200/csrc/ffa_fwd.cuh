@@ -20,6 +20,8 @@
 // versa.  The running max is rescaled lazily: O and l are rescaled only when a row's
 // max grows by more than 2^8, which keeps every P <= 256 (exact in fp32 / bf16 range).
 #pragma once
+#include <cstdlib>
+
 #include "ffa_common.cuh"
 
 namespace ffa {
@@ -32,6 +34,9 @@ constexpr int NTHREADS = 320;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int EMU_PAIRS = 0;  // of every 8 column pairs of an unmasked tile, exponentiated on the FMA pipe
+// (measured on B200 at B4 H16 S8192 D128 causal: 0 -> 1.12 ms, 2 -> 1.23 ms, 3 -> 1.36 ms;
+// the softmax is issue-bound, not MUFU-bound, so the FMA-pipe exp2 stays off by default)
 
 template <int D>
 struct Layout {
@@ -46,7 +51,7 @@ struct Layout {
 };
 }  // namespace fwd
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, int EMU = fwd::EMU_PAIRS>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ O,
@@ -76,19 +81,13 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   const int bh = blockIdx.y;
   const int m0 = mblk * 2 * fwd::BM;
   const int n_kv_all = (S + fwd::BN - 1) / fwd::BN;
-  int n_tiles[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int mi = m0 + i * fwd::BM;
-    if (mi >= S) {
-      n_tiles[i] = 0;
-    } else if (CAUSAL) {
-      n_tiles[i] = min(n_kv_all, (mi + fwd::BM - 1) / fwd::BN + 1);
-    } else {
-      n_tiles[i] = n_kv_all;
-    }
-  }
-  const int n_kv = max(n_tiles[0], n_tiles[1]);
+  // number of key tiles each 128-row query tile visits (0 for a tile past the end)
+  auto tiles_for = [&](int mi) {
+    if (mi >= S) return 0;
+    return CAUSAL ? min(n_kv_all, (mi + fwd::BM - 1) / fwd::BN + 1) : n_kv_all;
+  };
+  const int n_tiles0 = tiles_for(m0), n_tiles1 = tiles_for(m0 + fwd::BM);
+  const int n_kv = max(n_tiles0, n_tiles1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -157,13 +156,13 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16(128, fwd::BN, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
-      const uint32_t q_addr[2] = {sbase + L::Q_OFF, sbase + L::Q_OFF + L::TILE_BYTES};
+      const uint32_t q_addr0 = sbase + L::Q_OFF, q_addr1 = sbase + L::Q_OFF + L::TILE_BYTES;
       bool ok = mbar_wait(q_full, 0, abort_flag, kErrFwdMma);
       int it = 0;
       auto issue_qk = [&](int i, uint32_t k_addr) {
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tmem + i * 128, kmajor_desc(q_addr[i], 128, ks), kmajor_desc(k_addr, 128, ks), IDESC_QK,
+          mma_ss(tmem + i * 128, kmajor_desc(i ? q_addr1 : q_addr0, 128, ks), kmajor_desc(k_addr, 128, ks), IDESC_QK,
                  ks > 0);
         mma_commit(s_full(i));
       };
@@ -180,8 +179,8 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         if (ok) {
           tc_fence_after();
           const uint32_t k_addr = sbase + L::KV_OFF + s * L::TILE_BYTES;
-          if (n_tiles[0] > 0) issue_qk(0, k_addr);
-          if (n_tiles[1] > 0) issue_qk(1, k_addr);
+          if (n_tiles0 > 0) issue_qk(0, k_addr);
+          if (n_tiles1 > 0) issue_qk(1, k_addr);
           mma_commit(kv_empty(s));
           ++it;
         }
@@ -195,7 +194,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         int sk = -1;
         uint32_t k_addr = 0;
         // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
-        if (j < n_tiles[0]) {
+        if (j < n_tiles0) {
           if (!(ok = mbar_wait(p_ready(0), j & 1, abort_flag, kErrFwdMma))) break;
           tc_fence_after();
           issue_pv(0, v_addr, j);
@@ -205,17 +204,17 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
           if (!(ok = mbar_wait(kv_full(sk), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
           tc_fence_after();
           k_addr = sbase + L::KV_OFF + sk * L::TILE_BYTES;
-          if (j + 1 < n_tiles[0]) issue_qk(0, k_addr);
+          if (j + 1 < n_tiles0) issue_qk(0, k_addr);
         }
         // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
-        if (j < n_tiles[1]) {
+        if (j < n_tiles1) {
           if (!(ok = mbar_wait(p_ready(1), j & 1, abort_flag, kErrFwdMma))) break;
           tc_fence_after();
           issue_pv(1, v_addr, j);
         }
         mma_commit(kv_empty(sv));
         if (next) {
-          if (j + 1 < n_tiles[1]) issue_qk(1, k_addr);
+          if (j + 1 < n_tiles1) issue_qk(1, k_addr);
           mma_commit(kv_empty(sk));
           ++it;
         }
@@ -235,7 +234,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     const int row = (warp & 3) * 32 + lane;
     const int mi = m0 + i * fwd::BM;
     const int grow = mi + row;
-    const int nt = n_tiles[i];
+    const int nt = i ? n_tiles1 : n_tiles0;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + lane_off + i * 128;
     const uint32_t t_o = tmem + lane_off + 256 + i * 128;
@@ -254,19 +253,37 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]) * scale_log2;
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]);
       }
       const int n0 = j * fwd::BN;
       const bool need_mask = (n0 + fwd::BN > S) || (CAUSAL && n0 + fwd::BN - 1 > mi);
+      // Row max of the scaled scores.  Unmasked tiles reduce the raw scores and scale
+      // once (scale*log2e > 0 keeps the order; a negative scale reduces with min);
+      // masked tiles (diagonal / ragged tail) scale first and drop masked columns.
+      float tmax;
       if (need_mask) {
         const int lim = CAUSAL ? min(S - 1, grow) : (S - 1);
 #pragma unroll
-        for (int c = 0; c < fwd::BN; ++c)
-          if (n0 + c > lim) s[c] = -INFINITY;
-      }
-      float tmax = s[0];
+        for (int c = 0; c < fwd::BN; ++c) s[c] = (n0 + c > lim) ? -INFINITY : s[c] * scale_log2;
+        float a[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int c = 1; c < fwd::BN; ++c) tmax = fmaxf(tmax, s[c]);
+        for (int c = 4; c < fwd::BN; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) a[u] = fmax3(a[u], s[c + u], s[c + 4 + u]);
+        tmax = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+      } else if (scale_log2 >= 0.f) {
+        float a[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int c = 4; c < fwd::BN; c += 8)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) a[u] = fmax3(a[u], s[c + u], s[c + 4 + u]);
+        tmax = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * scale_log2;
+      } else {
+        float a = s[0];
+#pragma unroll
+        for (int c = 1; c < fwd::BN; ++c) a = fminf(a, s[c]);
+        tmax = a * scale_log2;
+      }
       const float m_new = fmaxf(m_used, tmax);
       const bool need = m_new > m_used + fwd::RESCALE_THRESHOLD;
       if (__any_sync(0xffffffffu, need)) {
@@ -289,14 +306,34 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       }
       const float m_safe = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t p[2][32];
-      float rowsum = 0.f;
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < fwd::BN / 2; ++c) {
-        const float p0 = fast_exp2(s[2 * c] - m_safe);
-        const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
-        rowsum += p0 + p1;
-        p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
+        for (int c = 0; c < fwd::BN / 2; ++c) {
+          const float p0 = fast_exp2(s[2 * c] - m_safe);
+          const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
+          sum[c & 3] += p0 + p1;
+          p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
+        }
+      } else {
+        // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
+#pragma unroll
+        for (int c = 0; c < fwd::BN / 2; ++c) {
+          const float x0 = fmaf(s[2 * c], scale_log2, -m_safe);
+          const float x1 = fmaf(s[2 * c + 1], scale_log2, -m_safe);
+          float p0, p1;
+          if ((c & 7) < EMU) {
+            p0 = exp2_fma(x0);
+            p1 = exp2_fma(x1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          sum[c & 3] += p0 + p1;
+          p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
+        }
       }
+      const float rowsum = (sum[0] + sum[1]) + (sum[2] + sum[3]);
       l += rowsum;
       tmem_st32(t_s, p[0]);
       tmem_st32(t_s + 32, p[1]);
@@ -346,7 +383,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 // host launcher
 // ------------------------------------------------------------------------------------
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, int EMU>
 static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   using L = fwd::Layout<D>;
   CUtensorMap tq, tk, tv;
@@ -354,7 +391,7 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  auto kern = ffa_fwd_kernel<D, CAUSAL>;
+  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
@@ -366,9 +403,31 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   return FFA_OK;
 }
 
+// Share of exponentials taken on the FMA pipe, in column pairs out of 8.  The default is
+// fwd::EMU_PAIRS; FFA_FWD_EMU=0..4 overrides it (for measurements only).
+static int fwd_emu_setting() {
+  static const int v = [] {
+    const char* e = std::getenv("FFA_FWD_EMU");
+    if (e == nullptr || e[0] < '0' || e[0] > '4' || e[1] != '\0') return fwd::EMU_PAIRS;
+    return e[0] - '0';
+  }();
+  return v;
+}
+
+template <int D, bool CAUSAL>
+static int launch_fwd_emu(const FwdArgs& a, cudaStream_t stream) {
+  switch (fwd_emu_setting()) {
+    case 0: return launch_fwd_t<D, CAUSAL, 0>(a, stream);
+    case 1: return launch_fwd_t<D, CAUSAL, 1>(a, stream);
+    case 3: return launch_fwd_t<D, CAUSAL, 3>(a, stream);
+    case 4: return launch_fwd_t<D, CAUSAL, 4>(a, stream);
+    default: return launch_fwd_t<D, CAUSAL, 2>(a, stream);
+  }
+}
+
 int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_fwd_t<128, true>(a, stream) : launch_fwd_t<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_fwd_t<64, true>(a, stream) : launch_fwd_t<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_fwd_emu<128, true>(a, stream) : launch_fwd_emu<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_fwd_emu<64, true>(a, stream) : launch_fwd_emu<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 

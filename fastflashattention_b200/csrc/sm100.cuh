@@ -285,10 +285,38 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 2^x on the special-function unit (MUFU.EX2).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, for x >= -126 (smaller x is clamped to -126; callers use it only
+// where no score is masked).  Method: Cody–Waite-style range reduction x = n + f with n
+// the nearest integer (obtained by adding and subtracting the shifter 1.5*2^23) and
+// f in [-1/2, 1/2]; 2^f from a degree-3 polynomial whose coefficients minimise the
+// maximum relative error on that interval (Remez exchange, derived by
+// csrc/fit_exp2_poly.py; max relative error 7.5e-5, 25x below bf16's half-ulp);
+// 2^n is applied by adding n to the exponent field.  Offloading part of the softmax
+// exponentials here keeps MUFU.EX2 (16/clk/SM) from capping the tensor core.
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kShifter = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.9999280571937561f, c1 = 0.6932609677314758f, c2 = 0.2426111251115799f,
+                  c3 = 0.0551716685295105f;
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, kShifter);  // low mantissa bits of t hold n = round(x)
+  const float n = __fsub_rn(t, kShifter);
+  const float f = __fsub_rn(x, n);
+  const float p = fmaf(fmaf(fmaf(c3, f, c2), f, c1), f, c0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Three-input max (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 }  // namespace ffa
