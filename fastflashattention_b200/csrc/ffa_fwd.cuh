@@ -13,6 +13,8 @@
 //   warps 4-7   softmax warpgroup for tile 1
 //   warp  8     TMA producer: Q0/Q1 once, then K_j, V_j through a 3-slot smem ring
 //   warp  9     MMA issuer (one thread): S_i = Q_i K_j^T  and  O_i += P_i V_j
+//   warps 10-11 idle (complete the third warpgroup, which hands its registers to the
+//               softmax warpgroups with setmaxnreg: 208 vs 88 registers per thread)
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512).
 // P_i (bf16, two per column) overwrites the first 64 columns of S_i and is the
 // A operand of the P.V MMA straight from tensor memory, so P never touches smem.
@@ -30,9 +32,14 @@ namespace fwd {
 constexpr int BM = 128;            // rows per Q tile (TMEM lanes)
 constexpr int BN = 128;            // keys per K/V tile
 constexpr int STAGES = 3;          // K/V smem ring slots
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 384;  // 3 warpgroups: softmax tile 0, softmax tile 1, producer + MMA (+2 idle)
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
+// Register split after launch (384 threads x 168 registers = 64512): the softmax
+// warpgroups hold a 128-float score row each and get 208, the producer/MMA warpgroup 88.
+constexpr int REGS_SOFTMAX = 208;
+constexpr int REGS_CONTROL = 88;
+constexpr int LAUNCH_REGS_NEEDED = (2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL) / NTHREADS;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr int EMU_PAIRS = 0;  // of every 8 column pairs of an unmasked tile, exponentiated on the FMA pipe
 // (measured on B200 at B4 H16 S8192 D128 causal: 0 -> 1.12 ms, 2 -> 1.23 ms, 3 -> 1.36 ms;
@@ -118,6 +125,10 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Each warpgroup changes its register budget inside its own branch, so the softmax
+  // code is compiled against 208 registers and the control code against 88.
+  if (warp >= 8) {
+  setmaxnreg_dec<fwd::REGS_CONTROL>();
   if (warp == fwd::PRODUCER_WARP) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
@@ -159,18 +170,23 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       const uint32_t q_addr0 = sbase + L::Q_OFF, q_addr1 = sbase + L::Q_OFF + L::TILE_BYTES;
       bool ok = mbar_wait(q_full, 0, abort_flag, kErrFwdMma);
       int it = 0;
+      // Descriptors are built once per tile / stage; a K-step only adds a constant.
+      const uint64_t qdesc0 = kmajor_desc(q_addr0, 128, 0), qdesc1 = kmajor_desc(q_addr1, 128, 0);
       auto issue_qk = [&](int i, uint32_t k_addr) {
+        const uint64_t qd = i ? qdesc1 : qdesc0;
+        const uint64_t kd = kmajor_desc(k_addr, 128, 0);
+        const uint32_t d = tmem + i * 128;
+        mma_ss(d, qd, kd, IDESC_QK, 0u);
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tmem + i * 128, kmajor_desc(i ? q_addr1 : q_addr0, 128, ks), kmajor_desc(k_addr, 128, ks), IDESC_QK,
-                 ks > 0);
+        for (int ks = 1; ks < D / 16; ++ks) mma_ss_acc(d, qd + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_QK);
         mma_commit(s_full(i));
       };
       auto issue_pv = [&](int i, uint32_t v_addr, int j) {
+        const uint64_t vd = mnmajor_desc(v_addr, fwd::BN, 0);
+        const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
+        mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < fwd::BN / 16; ++ks)
-          mma_ts(tmem + 256 + i * 128, tmem + i * 128 + ks * 8, mnmajor_desc(v_addr, fwd::BN, ks), IDESC_PV,
-                 (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 1; ks < fwd::BN / 16; ++ks) mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
       };
       // prologue: S_i(0)
       if (ok && n_kv > 0) {
@@ -228,7 +244,9 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       mbar_wait_drain(drain_bar, 0);
     }
     __syncwarp();
+  }
   } else {
+    setmaxnreg_inc<fwd::REGS_SOFTMAX>();
     // ------------------------------------------------------------------ softmax
     const int i = warp >> 2;            // tile
     const int row = (warp & 3) * 32 + lane;
@@ -394,6 +412,17 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   auto kern = ffa_fwd_kernel<D, CAUSAL, EMU>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
+  // The setmaxnreg split assumes the kernel is launched with 168 registers per thread;
+  // with fewer, setmaxnreg.inc could never be satisfied, so refuse to launch instead.
+  static int launch_regs = -1;
+  if (launch_regs < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kern)) != cudaSuccess)
+      return set_error(FFA_ERR_LAUNCH, "cudaFuncGetAttributes(fwd) failed");
+    launch_regs = fa.numRegs;
+  }
+  if (launch_regs < fwd::LAUNCH_REGS_NEEDED)
+    return set_error(FFA_ERR_LAUNCH, "forward kernel compiled with too few registers for its setmaxnreg split");
   const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
   kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(a.o), a.lse,
                                                         a.S, a.stride_bh, a.stride_s,

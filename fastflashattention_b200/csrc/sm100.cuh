@@ -182,6 +182,24 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       : "memory");
 }
 
+// Same, with the accumulate flag fixed to "accumulate" (no runtime predicate setup).
+__device__ __forceinline__ void mma_ss_acc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, 1, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, 1, 1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 operation issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -232,6 +250,17 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Warpgroup-wide register reallocation.  The sum over warpgroups after the change must not
+// exceed what the CTA was launched with (threads x registers per thread).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------------------------
 // Shared-memory matrix descriptors (tcgen05 version 1).
 //   bits  0-13 start address >> 4
@@ -268,6 +297,14 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_saddr, int rows, 
   const uint32_t addr = tile_saddr + ks * 16 * 128;
   return sw128_desc(addr, rows * 128, 1024);
 }
+
+// Descriptor increments (in the 16-byte units of the start-address field) that move a
+// base descriptor (ks = 0) to K-step ks; adding them never carries out of the 14-bit
+// field because shared-memory addresses stay below 2^18.
+__host__ __device__ constexpr uint32_t kmajor_step(int rows, int ks) {
+  return static_cast<uint32_t>(((ks >> 2) * rows * 128 + (ks & 3) * 32) >> 4);
+}
+__host__ __device__ constexpr uint32_t mnmajor_step(int ks) { return static_cast<uint32_t>((ks * 16 * 128) >> 4); }
 
 // Instruction descriptor, kind::f16 with bf16 inputs and fp32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format (1 = bf16), 10-12 B format (1 = bf16),
