@@ -20,11 +20,19 @@
 //              every step (thread = TMEM lane = one key / query row)
 //   warp  8    producer: TMA for the streamed tiles (and lse/delta for dkdv)
 //   warp  9    MMA issuer (one thread)
-// P and dS are written back over the columns they were computed from, as packed bf16
-// (warpgroup g's 64 values land in columns [64g, 64g+32) of the region), and feed the
-// gradient MMAs straight from tensor memory.
+// P and dS are written back to tensor memory as packed bf16 and feed the gradient MMAs
+// from there.  In the dq kernel dS overwrites the S columns it came from (warpgroup g's
+// 64 values land in [64g, 64g+32)).  In the dkdv kernel P and dS both go into the dP
+// columns once dP is in registers (warpgroup g: P at [64g, 64g+32), dS at
+// [64g+32, 64g+64) of the dP region), which frees the S columns for the next step's
+// S = K Q^T while this step's softmax is still running.
 #pragma once
 #include "ffa_common.cuh"
+
+// Timeline hook for measurement builds (see ffa_fwd.cuh); nothing in the library.
+#ifndef FFA_BWD_TRACE
+#define FFA_BWD_TRACE(site, step)
+#endif
 
 namespace ffa {
 
@@ -32,23 +40,35 @@ namespace bwd {
 constexpr int LANES = 128;   // TMEM lanes owned by a CTA
 constexpr int STEP = 128;    // width of one step along the streamed dimension
 constexpr int STAGES = 2;
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 384;  // 2 compute warpgroups + producer, MMA and 2 idle warps
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
+constexpr int DO_PRODUCER_WARP = 10;  // dkdv: the dO ring has its own producer
+// Register split after launch (384 x 168): compute warpgroups 208, control warpgroup 88.
+constexpr int REGS_COMPUTE = 208;
+constexpr int REGS_CONTROL = 88;
+constexpr int LAUNCH_REGS_NEEDED = (2 * 128 * REGS_COMPUTE + 128 * REGS_CONTROL) / NTHREADS;
 
 template <int D>
 struct DkdvLayout {
   static constexpr int TILE = 128 * D * 2;  // K, V (resident) and Q, dO (streamed) tiles
+  // Q_i is read by S(i) (issued a step early) and by dK(i) (at the end of step i), dO_i
+  // by dP(i) and dV(i) within one step: three Q slots and two dO slots.
+  static constexpr int Q_STAGES = 3;
+  static constexpr int DO_STAGES = 2;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE;
-  static constexpr int STAGE_OFF = 2 * TILE;
-  // stage: Q tile, dO tile, lse[128], delta[128]
-  static constexpr int STAGE_BYTES = ((2 * TILE + 2 * STEP * 4) + 1023) / 1024 * 1024;
-  static constexpr int BAR_OFF = STAGE_OFF + STAGES * STAGE_BYTES;
-  // kv_full, st_full[2], st_empty[2], s_full, dp_full, p_ready, ds_ready, final, drain
-  static constexpr int NBARS = 1 + 2 * STAGES + 6;
+  static constexpr int Q_OFF = 2 * TILE;
+  static constexpr int DO_OFF = Q_OFF + Q_STAGES * TILE;
+  static constexpr int DO_STAGE_BYTES = TILE + 2 * STEP * 4;  // dO tile, lse[128], delta[128]
+  static constexpr int BAR_OFF = DO_OFF + DO_STAGES * DO_STAGE_BYTES;
+  // kv_full, q_full[3], q_empty[3], do_full[2], do_empty[2], s_full, dp_full, p_ready,
+  // ds_ready, final, drain, s_free
+  static constexpr int NBARS = 1 + 2 * Q_STAGES + 2 * DO_STAGES + 7;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
+  // no alignment slack: the kernel declares its dynamic shared memory 1024-byte aligned
+  // (and checks it), which is what lets this layout fit in 227 KB
+  static constexpr int SMEM_BYTES = MISC_OFF + 16;
 };
 
 template <int D>
@@ -120,22 +140,34 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
                         long long stride_s, float scale_log2, float scale) {
   using L = bwd::DkdvLayout<D>;
   constexpr int SLABS = D / 64;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if (smem_u32(smem) & 1023u) {  // the layout has no room to realign: report and leave
+    if (threadIdx.x == 0) atomicCAS(&g_status[0], 0u, static_cast<unsigned int>(kErrBwdAlign));
+    return;
+  }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::BAR_OFF;
+  constexpr int QS = L::Q_STAGES, DS = L::DO_STAGES;
   const uint32_t kv_full = bar0;
-  auto st_full = [&](int s) { return bar0 + 8 * (1 + s); };
-  auto st_empty = [&](int s) { return bar0 + 8 * (1 + bwd::STAGES + s); };
-  const uint32_t s_full = bar0 + 8 * (1 + 2 * bwd::STAGES);
+  auto q_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto q_empty = [&](int s) { return bar0 + 8 * (1 + QS + s); };
+  auto do_full = [&](int s) { return bar0 + 8 * (1 + 2 * QS + s); };
+  auto do_empty = [&](int s) { return bar0 + 8 * (1 + 2 * QS + DS + s); };
+  const uint32_t s_full = bar0 + 8 * (1 + 2 * QS + 2 * DS);
   const uint32_t dp_full = s_full + 8;
   const uint32_t p_ready = s_full + 16;
   const uint32_t ds_ready = s_full + 24;
   const uint32_t final_bar = s_full + 32;
   const uint32_t drain_bar = s_full + 40;
+  const uint32_t s_free = s_full + 48;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
-  auto stage_ptr = [&](int s) { return smem + L::STAGE_OFF + s * L::STAGE_BYTES; };
+  auto q_addr = [&](int i) { return sbase + L::Q_OFF + (i % QS) * L::TILE; };
+  auto do_addr = [&](int i) { return sbase + L::DO_OFF + (i % DS) * L::DO_STAGE_BYTES; };
+  auto lse_smem = [&](int i) {
+    return reinterpret_cast<float*>(smem + L::DO_OFF + (i % DS) * L::DO_STAGE_BYTES + L::TILE);
+  };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -147,11 +179,16 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < bwd::STAGES; ++s) {
-      mbar_init(st_full(s), 2);  // TMA expect-tx arrival + lse/delta arrival
-      mbar_init(st_empty(s), 1);
+    for (int s = 0; s < QS; ++s) {
+      mbar_init(q_full(s), 1);
+      mbar_init(q_empty(s), 1);
+    }
+    for (int s = 0; s < DS; ++s) {
+      mbar_init(do_full(s), 2);  // TMA expect-tx arrival + lse/delta arrival
+      mbar_init(do_empty(s), 1);
     }
     mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
     mbar_init(dp_full, 1);
     mbar_init(p_ready, 256);
     mbar_init(ds_ready, 256);
@@ -175,33 +212,47 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
+  setmaxnreg_dec<bwd::REGS_CONTROL>();
   if (warp == bwd::PRODUCER_WARP) {
-    // ---------------------------------------------------------------- producer
-    const uint64_t keep = policy_evict_last();
+    // ---------------------------------------------------------------- producer: K, V, Q ring
     if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
       mbar_arrive_expect_tx(kv_full, 2 * L::TILE);
       for (int sl = 0; sl < SLABS; ++sl) {
         tma_load_3d(sbase + L::K_OFF + sl * 16384, &tm_k, kv_full, sl * 64, n0, bh, keep);
         tma_load_3d(sbase + L::V_OFF + sl * 16384, &tm_v, kv_full, sl * 64, n0, bh, keep);
       }
+      int issued = 0;
+      for (int it = 0; it < nq; ++it) {
+        const int s = it % QS;
+        if (!mbar_wait(q_empty(s), ((it / QS) & 1) ^ 1, abort_flag, kErrBwdProducer)) break;
+        mbar_arrive_expect_tx(q_full(s), L::TILE);
+        for (int sl = 0; sl < SLABS; ++sl)
+          tma_load_3d(q_addr(it) + sl * 16384, &tm_q, q_full(s), sl * 64, q_begin + it * bwd::STEP, bh, keep);
+        ++issued;
+      }
+      if (*abort_flag) {
+        mbar_wait_drain(kv_full, 0);
+        for (int it = max(0, issued - QS); it < issued; ++it) mbar_wait_drain(q_full(it % QS), (it / QS) & 1);
+      }
     }
+  } else if (warp == bwd::DO_PRODUCER_WARP) {
+    // ---------------------------------------------------------------- producer: dO ring + lse/delta
+    const uint64_t keep = policy_evict_last();
     int issued = 0;
     for (int it = 0; it < nq; ++it) {
-      const int s = it % bwd::STAGES;
+      const int s = it % DS;
       bool ok = true;
-      if (lane == 0) ok = mbar_wait(st_empty(s), ((it / bwd::STAGES) & 1) ^ 1, abort_flag, kErrBwdProducer);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (lane == 0) ok = mbar_wait(do_empty(s), ((it / DS) & 1) ^ 1, abort_flag, kErrBwdProducer);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       const int q0 = q_begin + it * bwd::STEP;
-      const uint32_t st = smem_u32(stage_ptr(s));
       if (lane == 0) {
-        mbar_arrive_expect_tx(st_full(s), 2 * L::TILE);
-        for (int sl = 0; sl < SLABS; ++sl) {
-          tma_load_3d(st + sl * 16384, &tm_q, st_full(s), sl * 64, q0, bh, keep);
-          tma_load_3d(st + L::TILE + sl * 16384, &tm_do, st_full(s), sl * 64, q0, bh, keep);
-        }
+        mbar_arrive_expect_tx(do_full(s), L::TILE);
+        for (int sl = 0; sl < SLABS; ++sl)
+          tma_load_3d(do_addr(it) + sl * 16384, &tm_do, do_full(s), sl * 64, q0, bh, keep);
       }
-      float* lse_s = reinterpret_cast<float*>(stage_ptr(s) + 2 * L::TILE);
+      float* lse_s = lse_smem(it);
       float* dl_s = lse_s + bwd::STEP;
 #pragma unroll
       for (int r = lane; r < bwd::STEP; r += 32) {
@@ -212,23 +263,19 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         dl_s[r] = (q < S) ? DELTA[idx] : 0.f;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(st_full(s));
+      if (lane == 0) mbar_arrive(do_full(s));
       ++issued;
     }
-    if (lane == 0 && *abort_flag) {
-      mbar_wait_drain(kv_full, 0);
-      for (int it = max(0, issued - bwd::STAGES); it < issued; ++it)
-        mbar_wait_drain(st_full(it % bwd::STAGES), (it / bwd::STAGES) & 1);
-    }
+    if (lane == 0 && *abort_flag)
+      for (int it = max(0, issued - DS); it < issued; ++it) mbar_wait_drain(do_full(it % DS), (it / DS) & 1);
   } else if (warp == bwd::MMA_WARP) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_SD = idesc_bf16(128, bwd::STEP, false, false);  // [128 keys x 128 queries]
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);            // [128 keys x D]
       const uint32_t k_addr = sbase + L::K_OFF, v_addr = sbase + L::V_OFF;
-      auto q_addr = [&](int i) { return smem_u32(stage_ptr(i % bwd::STAGES)); };
       auto issue_s = [&](int i) -> bool {  // S^T = K Q_i^T
-        if (!mbar_wait(st_full(i % bwd::STAGES), (i / bwd::STAGES) & 1, abort_flag, kErrBwdMma)) return false;
+        if (!mbar_wait(q_full(i % QS), (i / QS) & 1, abort_flag, kErrBwdMma)) return false;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
@@ -236,19 +283,21 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         mma_commit(s_full);
         return true;
       };
-      auto issue_dp = [&](int i) {  // dP^T = V dO_i^T
+      auto issue_dp = [&](int i) -> bool {  // dP^T = V dO_i^T
+        if (!mbar_wait(do_full(i % DS), (i / DS) & 1, abort_flag, kErrBwdMma)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks)
-          mma_ss(tmem + 128, kmajor_desc(v_addr, 128, ks), kmajor_desc(q_addr(i) + L::TILE, 128, ks), IDESC_SD,
-                 ks > 0);
+          mma_ss(tmem + 128, kmajor_desc(v_addr, 128, ks), kmajor_desc(do_addr(i), 128, ks), IDESC_SD, ks > 0);
         mma_commit(dp_full);
+        return true;
       };
       auto issue_dv = [&](int i) -> bool {  // dV += P^T dO_i
         if (!mbar_wait(p_ready, i & 1, abort_flag, kErrBwdMma)) return false;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < bwd::STEP / 16; ++ks)
-          mma_ts(tmem + 256, bwd::packed_kstep_col(tmem, ks), mnmajor_desc(q_addr(i) + L::TILE, 128, ks), IDESC_G,
+          mma_ts(tmem + 256, bwd::packed_kstep_col(tmem + 128, ks), mnmajor_desc(do_addr(i), 128, ks), IDESC_G,
                  (i > 0 || ks > 0) ? 1u : 0u);
         return true;
       };
@@ -257,30 +306,43 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < bwd::STEP / 16; ++ks)
-          mma_ts(tmem + 384, bwd::packed_kstep_col(tmem + 128, ks), mnmajor_desc(q_addr(i), 128, ks), IDESC_G,
+          mma_ts(tmem + 384, bwd::packed_kstep_col(tmem + 128 + 32, ks), mnmajor_desc(q_addr(i), 128, ks), IDESC_G,
                  (i > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(st_empty(i % bwd::STAGES));
+        mma_commit(q_empty(i % QS));
+        mma_commit(do_empty(i % DS));
         return true;
       };
       bool ok = mbar_wait(kv_full, 0, abort_flag, kErrBwdMma);
       if (ok && nq > 0) {
         ok = issue_s(0);
-        if (ok) issue_dp(0);
+        if (ok) ok = issue_dp(0);
       }
-      // dV(i), S(i+1), dK(i), dP(i+1): the next step's S and dP run while the
-      // warpgroups turn this step's dP into dS and the next step's S into P.
+      // S(i+1) as soon as the warpgroups have copied S(i) into registers, then dV(i),
+      // dK(i) and dP(i+1): P(i) and dS(i) live in the dP columns, so the next step's
+      // scores are computed during this step's whole softmax.
       for (int i = 0; i < nq && ok; ++i) {
+        FFA_BWD_TRACE(0, i);
+        if (i + 1 < nq) {
+          if (!(ok = mbar_wait(s_free, i & 1, abort_flag, kErrBwdMma))) break;
+          tc_fence_after();
+          if (!(ok = issue_s(i + 1))) break;
+        }
+        FFA_BWD_TRACE(1, i);
         if (!(ok = issue_dv(i))) break;
-        if (i + 1 < nq && !(ok = issue_s(i + 1))) break;
+        FFA_BWD_TRACE(2, i);
         if (!(ok = issue_dk(i))) break;
-        if (i + 1 < nq) issue_dp(i + 1);
+        FFA_BWD_TRACE(3, i);
+        if (i + 1 < nq && !(ok = issue_dp(i + 1))) break;
+        FFA_BWD_TRACE(4, i);
       }
       if (ok) mma_commit(final_bar);
       mma_commit(drain_bar);
       mbar_wait_drain(drain_bar, 0);
     }
     __syncwarp();
+  }
   } else {
+    setmaxnreg_inc<bwd::REGS_COMPUTE>();
     // ---------------------------------------------------------------- compute
     const int g = warp >> 2;                  // warpgroup: query columns [64g, 64g+64) of a step
     const int row = (warp & 3) * 32 + lane;   // key row within the block
@@ -290,23 +352,32 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     const uint32_t t_dp = tmem + lane_off + 128 + 64 * g;
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
-      const float* lse_s = reinterpret_cast<const float*>(stage_ptr(i % bwd::STAGES) + 2 * L::TILE) + 64 * g;
-      const float* dl_s = lse_s + bwd::STEP;
       const int qc = q_begin + i * bwd::STEP + 64 * g;  // first query of this thread's columns
+      // lse / delta of this step (written next to dO_i by the dO producer)
+      if (!(ok = mbar_wait(do_full(i % DS), (i / DS) & 1, abort_flag, kErrBwdCompute))) break;
+      const float* lse_s = lse_smem(i) + 64 * g;
+      const float* dl_s = lse_s + bwd::STEP;
       float p[64];
       if (!(ok = mbar_wait(s_full, i & 1, abort_flag, kErrBwdCompute))) break;
+      if (threadIdx.x == 0) FFA_BWD_TRACE(8, i);
       tc_fence_after();
       bwd::tmem_ld64(t_s, p);
+      tc_fence_before();
+      mbar_arrive(s_free);  // S may now be overwritten by S(i+1)
+      if (threadIdx.x == 0) FFA_BWD_TRACE(12, i);
+      uint32_t pk[32];
       {
         const bool need_mask = CAUSAL && (qc < kg);  // some query of these columns precedes the key
-        uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 64; e += 4) {
           const float4 l4 = *reinterpret_cast<const float4*>(lse_s + e);
-          p[e + 0] = fast_exp2(fmaf(p[e + 0], scale_log2, -l4.x));
-          p[e + 1] = fast_exp2(fmaf(p[e + 1], scale_log2, -l4.y));
-          p[e + 2] = fast_exp2(fmaf(p[e + 2], scale_log2, -l4.z));
-          p[e + 3] = fast_exp2(fmaf(p[e + 3], scale_log2, -l4.w));
+          const float2 c2 = make_float2(scale_log2, scale_log2);
+          const float2 xa = fma2(make_float2(p[e], p[e + 1]), c2, make_float2(-l4.x, -l4.y));
+          const float2 xb = fma2(make_float2(p[e + 2], p[e + 3]), c2, make_float2(-l4.z, -l4.w));
+          p[e + 0] = fast_exp2(xa.x);
+          p[e + 1] = fast_exp2(xa.y);
+          p[e + 2] = fast_exp2(xb.x);
+          p[e + 3] = fast_exp2(xb.y);
           if (need_mask) {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
@@ -315,27 +386,45 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           pk[e / 2] = pack_bf16x2(p[e], p[e + 1]);
           pk[e / 2 + 1] = pack_bf16x2(p[e + 2], p[e + 3]);
         }
-        tmem_st32(t_s, pk);
-        tmem_st_wait();
       }
-      tc_fence_before();
-      mbar_arrive(p_ready);
+      if (threadIdx.x == 0) FFA_BWD_TRACE(14, i);
       if (!(ok = mbar_wait(dp_full, i & 1, abort_flag, kErrBwdCompute))) break;
+      if (threadIdx.x == 0) FFA_BWD_TRACE(10, i);
       tc_fence_after();
+      // dP(i) comes into registers half by half; its columns then take P(i) (first half)
+      // and dS(i) (second half), so at most P, packed P and 32 dP values are live at once
+      uint32_t dlo[32], dhi[32];
+      tmem_ld32(t_dp, dlo);
+      tmem_ld_wait();
+      tmem_st32(t_dp, pk);
+      tmem_ld32(t_dp + 32, dhi);
+      tmem_ld_wait();
+      tmem_st_wait();
+      if (threadIdx.x == 0) FFA_BWD_TRACE(13, i);
+      tc_fence_before();
+      if (threadIdx.x == 0) FFA_BWD_TRACE(9, i);
+      mbar_arrive(p_ready);
       {
-        float dp[64];
-        bwd::tmem_ld64(t_dp, dp);
         uint32_t dk[32];
 #pragma unroll
         for (int e = 0; e < 64; e += 4) {
           const float4 d4 = *reinterpret_cast<const float4*>(dl_s + e);
-          dk[e / 2] = pack_bf16x2(p[e] * (dp[e] - d4.x), p[e + 1] * (dp[e + 1] - d4.y));
-          dk[e / 2 + 1] = pack_bf16x2(p[e + 2] * (dp[e + 2] - d4.z), p[e + 3] * (dp[e + 3] - d4.w));
+          const uint32_t* src = (e < 32) ? dlo : dhi;
+          const int b = e & 31;
+          const float2 da = mul2(make_float2(p[e], p[e + 1]),
+                                 sub2(make_float2(__uint_as_float(src[b]), __uint_as_float(src[b + 1])),
+                                      make_float2(d4.x, d4.y)));
+          const float2 db = mul2(make_float2(p[e + 2], p[e + 3]),
+                                 sub2(make_float2(__uint_as_float(src[b + 2]), __uint_as_float(src[b + 3])),
+                                      make_float2(d4.z, d4.w)));
+          dk[e / 2] = pack_bf16x2(da.x, da.y);
+          dk[e / 2 + 1] = pack_bf16x2(db.x, db.y);
         }
-        tmem_st32(t_dp, dk);
+        tmem_st32(t_dp + 32, dk);
         tmem_st_wait();
       }
       tc_fence_before();
+      if (threadIdx.x == 0) FFA_BWD_TRACE(11, i);
       mbar_arrive(ds_ready);
     }
     if (ok && nq > 0 && mbar_wait(final_bar, 0, abort_flag, kErrBwdCompute)) {
@@ -431,6 +520,8 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
+  setmaxnreg_dec<bwd::REGS_CONTROL>();
   if (warp == bwd::PRODUCER_WARP) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
@@ -521,7 +612,9 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       mbar_wait_drain(drain_bar, 0);
     }
     __syncwarp();
+  }
   } else {
+    setmaxnreg_inc<bwd::REGS_COMPUTE>();
     // ---------------------------------------------------------------- compute
     const int g = warp >> 2;
     const int row = (warp & 3) * 32 + lane;  // query row within the block
@@ -545,15 +638,19 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       const int kc = j * bwd::STEP + 64 * g;  // first key of this thread's columns
       const bool need_mask = (kc + 64 > S) || (CAUSAL && kc + 63 > qg);
       uint32_t dsp[32];
+      const float2 c2 = make_float2(scale_log2, scale_log2), l2 = make_float2(-lse, -lse);
+      const float2 d2 = make_float2(dl, dl);
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
-        float p0 = fast_exp2(fmaf(sv[e], scale_log2, -lse));
-        float p1 = fast_exp2(fmaf(sv[e + 1], scale_log2, -lse));
+        const float2 x = fma2(make_float2(sv[e], sv[e + 1]), c2, l2);
+        float p0 = fast_exp2(x.x);
+        float p1 = fast_exp2(x.y);
         if (need_mask) {
           if (kc + e > lim) p0 = 0.f;
           if (kc + e + 1 > lim) p1 = 0.f;
         }
-        dsp[e >> 1] = pack_bf16x2(p0 * (dp[e] - dl), p1 * (dp[e + 1] - dl));
+        const float2 ds = mul2(make_float2(p0, p1), sub2(make_float2(dp[e], dp[e + 1]), d2));
+        dsp[e >> 1] = pack_bf16x2(ds.x, ds.y);
       }
       tmem_st32(tmem + lane_off + dq_sbuf(b) + 64 * g, dsp);
       tmem_st_wait();
@@ -590,6 +687,7 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   auto kern = ffa_bwd_dkdv_kernel<D, CAUSAL>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LK::SMEM_BYTES, &configured))) return rc;
+  if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
   kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, a.lse, a.delta,
                                                         static_cast<__nv_bfloat16*>(a.dk),
@@ -613,6 +711,7 @@ static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   auto kern = ffa_bwd_dq_kernel<D, CAUSAL>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
+  if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
   kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, a.lse, a.delta,
                                                         static_cast<__nv_bfloat16*>(a.dq), a.S, a.stride_bh,

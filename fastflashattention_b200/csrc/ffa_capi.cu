@@ -122,6 +122,14 @@ static int noalloc_delta_ptr(float** out) {
   return FFA_OK;
 }
 
+int check_launch_regs(const void* kernel, int needed) {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaFuncGetAttributes failed");
+  if (fa.numRegs < needed)
+    return set_error(FFA_ERR_LAUNCH, "kernel compiled with too few registers for its setmaxnreg split");
+  return FFA_OK;
+}
+
 // Shape / stride / alignment checks shared by the entry points.
 static int check_common(int BH, int S, int D, long long stride_bh, long long stride_s) {
   if (BH < 0 || S < 0) return set_error(FFA_ERR_INVALID, "BH and S must be non-negative");

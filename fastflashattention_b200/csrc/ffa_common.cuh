@@ -21,6 +21,7 @@ enum : unsigned int {
   kErrBwdProducer = 0x201,
   kErrBwdMma = 0x202,
   kErrBwdCompute = 0x203,
+  kErrBwdAlign = 0x204,  // dynamic shared memory not 1024-byte aligned
   kErrDqProducer = 0x301,
   kErrDqMma = 0x302,
   kErrDqCompute = 0x303,
@@ -61,6 +62,9 @@ int ensure_context();
 // Raise a kernel's dynamic shared-memory limit once per device; `done` is a per-kernel
 // bitmask of devices already configured.
 int set_smem_once(const void* kernel, int bytes, unsigned long long* done);
+// FFA_OK if `kernel` is launched with at least `needed` registers per thread (kernels
+// that rebalance registers with setmaxnreg rely on the launch allocation).
+int check_launch_regs(const void* kernel, int needed);
 // 3-D tensor map over a [BH, S, D] bf16 tensor: box = 64 columns x `box_rows` rows x 1
 // slice, 128-byte swizzle (the layout the tcgen05 descriptors in sm100.cuh expect).
 int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,

@@ -335,10 +335,11 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         }
       } else {
         // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
+        const float2 c2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m_safe, -m_safe);
 #pragma unroll
         for (int c = 0; c < fwd::BN / 2; ++c) {
-          const float x0 = fmaf(s[2 * c], scale_log2, -m_safe);
-          const float x1 = fmaf(s[2 * c + 1], scale_log2, -m_safe);
+          const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), c2, nm2);
+          const float x0 = x.x, x1 = x.y;
           float p0, p1;
           if ((c & 7) < EMU) {
             p0 = exp2_fma(x0);
