@@ -354,6 +354,71 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_ring(args, rank, world, local_rank):
+    """Context-parallel ring: the sequence (B1 H32 S131072 D128 causal unless overridden)
+    is split zig-zag over the ranks; value = whole-sequence fwd+bwd FLOPs / max-rank time."""
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, str(ROOT))
+    from fastflashattention_b200 import _lib, ring
+
+    B, H, S, D = 1, 32, 131072, 128
+    if args.S != 8192:
+        S = args.S
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    try:
+        C2 = S // world
+        gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+        mk = lambda: torch.randn(B, H, C2, D, device=dev, dtype=torch.bfloat16, generator=gen)  # noqa: E731
+        q, k, v, do = mk(), mk(), mk(), mk()
+        qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+
+        if world > 1:
+            def step():
+                o = ring.ring_attention(qg, kg, vg)
+                return torch.autograd.grad(o, (qg, kg, vg), do)
+        else:
+            from fastflashattention_b200 import fast_attention
+
+            def step():
+                o = fast_attention(qg, kg, vg, is_causal=True)
+                return torch.autograd.grad(o, (qg, kg, vg), do)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        _, step_flops = attn_flops(B, H, S, D, True)
+        if rank == 0:
+            print(json.dumps({
+                "metric": METRIC + " [context-parallel ring]", "value": step_flops / (ms / 1e3) / 1e12, "unit": UNIT,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic N(0,1) bf16 inputs, seeded",
+                "config": {"workload": f"B{B} H{H} S{S} D{D} causal fwd+bwd, sequence split zig-zag over {world} GPUs",
+                           "parallelism": f"cp{world} (ring: NCCL send/recv of K/V and dK/dV)"},
+                "device_status": list(_lib.device_status())}), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -366,6 +431,9 @@ def main():
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["shard", "ring"], default="shard",
+                    help="shard: batch x head data parallel (default workload); ring: context-parallel ring "
+                         "over the sequence (BASELINE configs[4]: B1 H32 S131072 D128)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -374,6 +442,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.mode == "ring":
+        return run_ring(args, rank, world, local_rank)
     if world > 1:
         import torch
         import torch.distributed as dist
