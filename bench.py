@@ -37,9 +37,9 @@ UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM bytes (read + write) per launch of the dK/dV kernel, from the ncu capture
-# summarised in profiles/bwd_dkdv_b2h16s8192d128_causal.md (B2 H16 = 32 slices), scaled to the
+# summarised in profiles/kernels_b2h16s8192d128_causal.md (B2 H16 = 32 slices), scaled to the
 # bench's (batch, head) slice count.
-DKDV_DRAM_BYTES_PER_SLICE = (270.6432e6 + 106.433536e6) / 32
+DKDV_DRAM_BYTES_PER_SLICE = (270.692096e6 + 107.322624e6) / 32
 
 
 def attn_flops(B, H, S, D, causal):
@@ -57,20 +57,48 @@ def load_peaks():
 
 # ------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons of one GPU while running."""
+    """Samples the SM clock, power and clock-event reasons of one GPU while running.
+
+    NVML is polled every 2 ms from a thread (the timed region of a step is tens of
+    milliseconds, shorter than nvidia-smi's loop period); without NVML, nvidia-smi -lms
+    100 is read instead.  Every sample carries a host timestamp and ``stop`` keeps the
+    ones inside the window marked by ``begin()`` / ``end()``, the timed region.
+    """
 
     FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, bus_id: str | None, fallback_index: int = 0):
         self.bus_id = (bus_id or "").lower()
         self.fallback_index = str(fallback_index)
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, float, float, tuple]] = []  # t, sm, max, W, reasons
+        self.lines: list[tuple[float, str]] = []
         self._t = None
+        self._stop = threading.Event()
+        self._nvml = None
+        self.window = (0.0, float("inf"))
+        self.source = None
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(self.bus_id.upper()) if self.bus_id else None
+            except pynvml.NVMLError:
+                h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(int(self.fallback_index))
+            self._nvml = (pynvml, h)
+            self.source = "nvml 2 ms"
+            self._t = threading.Thread(target=self._poll_nvml, daemon=True)
+            self._t.start()
+            return
+        except Exception:  # noqa: BLE001 - no NVML: fall back to nvidia-smi
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
@@ -78,37 +106,70 @@ class ClockSampler:
         except (FileNotFoundError, OSError):
             self.proc = None
             return
+        self.source = "nvidia-smi 100 ms"
         self._t = threading.Thread(target=self._read, daemon=True)
         self._t.start()
 
+    def _poll_nvml(self):
+        nv, h = self._nvml
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                w = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                names = tuple(n for n, b in zip(self.REASONS, bits) if r & b)
+                self.samples.append((time.monotonic(), sm, mx, w, names))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def begin(self):
+        self.window = (time.monotonic(), float("inf"))
+
+    def end(self):
+        self.window = (self.window[0], time.monotonic())
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         if self._t:
             self._t.join(timeout=2)
-        allrows = [p for p in ([x.strip() for x in ln.split(",")] for ln in self.lines) if len(p) >= 10]
-        rows = [p for p in allrows if self.bus_id and p[1].lower().endswith(self.bus_id[-7:])]
-        if not rows:  # bus id unknown or not matched: nvidia-smi index of the local device
-            rows = [p for p in allrows if p[0] == self.fallback_index]
-        if not rows:
+        if self.proc is not None:
+            allrows = [(t, [x.strip() for x in ln.split(",")]) for t, ln in self.lines]
+            allrows = [(t, p) for t, p in allrows if len(p) >= 10]
+            rows = [(t, p) for t, p in allrows if self.bus_id and p[1].lower().endswith(self.bus_id[-7:])]
+            if not rows:  # bus id unknown or not matched: nvidia-smi index of the local device
+                rows = [(t, p) for t, p in allrows if p[0] == self.fallback_index]
+            for t, r in rows:
+                if r[2].replace(".", "").isdigit() and r[3].replace(".", "").isdigit():
+                    w = float(r[4]) if r[4].replace(".", "").isdigit() else 0.0
+                    names = tuple(n for i, n in enumerate(self.REASONS) if r[6 + i].lower() == "active")
+                    self.samples.append((t, float(r[2]), float(r[3]), w, names))
+        if not self.samples:
             return None
-        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        mx = max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
-        loaded = [x for x in sm if x > 0.5 * mx] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[4]) for r in rows
-                                                         if r[4].replace(".", "").isdigit())}
+        lo, hi = self.window
+        inside = [x for x in self.samples if lo <= x[0] <= hi]
+        rows = inside or self.samples
+        mx = max(x[2] for x in rows)
+        sm = [x[1] for x in rows]
+        loaded = [v for v in sm if v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted({n for x in rows for n in x[4]}),
+                "samples": len(rows), "in_timed_region": bool(inside),
+                "power_w_median": round(statistics.median(x[3] for x in rows), 1),
+                "power_w_max": round(max(x[3] for x in rows), 1), "source": self.source}
 
 
 def pci_bus_string(props):
@@ -216,11 +277,13 @@ def run_ours(args, rank, world, local_rank):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    sampler.begin()
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
     torch.cuda.synchronize()
+    sampler.end()
     barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop()
@@ -288,22 +351,39 @@ def run_ours(args, rank, world, local_rank):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
-        gq, gk, gv = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, k, v))
-        dq_in, dk_in, dv_in, ddo = (torch.empty_like(q) for _ in range(4))
+        # The step is split into head chunks on their own streams, so the upload of one
+        # chunk and the download of another overlap the attention of a third (H2D and
+        # D2H use separate copy engines).  Every byte still crosses PCIe every step.
+        BHn = B * H
+        flat = lambda t: t.reshape(1, BHn, S, D)  # noqa: E731
+        hq, hk, hv, hdo = (flat(t).cpu().pin_memory() for t in (q, k, v, do))
+        gq, gk, gv = (torch.empty(hq.shape, dtype=q.dtype, pin_memory=True) for _ in range(3))
+        dq_in, dk_in, dv_in, ddo = (torch.empty((1, BHn, S, D), device=dev, dtype=q.dtype) for _ in range(4))
+        n_chunks = min(4, BHn)
+        bounds = [BHn * c // n_chunks for c in range(n_chunks + 1)]
+        streams = [torch.cuda.Stream(device=dev) for _ in range(n_chunks)]
 
         def e2e_step():
-            with torch.no_grad():
-                dq_in.copy_(hq, non_blocking=True)
-                dk_in.copy_(hk, non_blocking=True)
-                dv_in.copy_(hv, non_blocking=True)
-                ddo.copy_(hdo, non_blocking=True)
-            a_, b_, c_ = (t.detach().requires_grad_(True) for t in (dq_in, dk_in, dv_in))
-            o_ = fast_attention(a_, b_, c_, is_causal=causal)
-            g = torch.autograd.grad(o_, (a_, b_, c_), ddo)
-            gq.copy_(g[0], non_blocking=True)
-            gk.copy_(g[1], non_blocking=True)
-            gv.copy_(g[2], non_blocking=True)
+            start = torch.cuda.Event()
+            start.record(stream)
+            done = []
+            for c, cs in enumerate(streams):
+                h0, h1 = bounds[c], bounds[c + 1]
+                cs.wait_event(start)
+                with torch.cuda.stream(cs):
+                    with torch.no_grad():
+                        for dst, src in ((dq_in, hq), (dk_in, hk), (dv_in, hv), (ddo, hdo)):
+                            dst[:, h0:h1].copy_(src[:, h0:h1], non_blocking=True)
+                    a_, b_, c_ = (t[:, h0:h1].detach().requires_grad_(True) for t in (dq_in, dk_in, dv_in))
+                    o_ = fast_attention(a_, b_, c_, is_causal=causal)
+                    g = torch.autograd.grad(o_, (a_, b_, c_), ddo[:, h0:h1])
+                    for dst, src in ((gq, g[0]), (gk, g[1]), (gv, g[2])):
+                        dst[:, h0:h1].copy_(src, non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    done.append(ev)
+            for ev in done:
+                stream.wait_event(ev)
 
         for _ in range(2):
             e2e_step()
@@ -323,7 +403,8 @@ def run_ours(args, rank, world, local_rank):
         nbytes = q.numel() * q.element_size()
         e2e = {"value": world * step_flops / (ems / 1e3) / 1e12, "unit": UNIT, "ms_per_step": ems,
                "h2d_bytes_per_step": 4 * nbytes * world, "d2h_bytes_per_step": 3 * nbytes * world,
-               "path": "pinned host q,k,v,dO -> fast_attention fwd + autograd bwd -> dq,dk,dv to pinned host"}
+               "path": "pinned host q,k,v,dO -> fast_attention fwd + autograd bwd -> dq,dk,dv to pinned host",
+               "pipelining": f"{n_chunks} head chunks on {n_chunks} streams (copies overlap compute)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -390,14 +471,20 @@ def run_ring(args, rank, world, local_rank):
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
+        sampler = ClockSampler(pci_bus_string(torch.cuda.get_device_properties(dev)), local_rank)
+        sampler.start()
+        time.sleep(0.1)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler.begin()
         e0.record()
         for _ in range(args.steps):
             step()
         e1.record()
         torch.cuda.synchronize()
+        sampler.end()
+        clocks = sampler.stop()
         ms = e0.elapsed_time(e1) / args.steps
         if world > 1:
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -412,7 +499,7 @@ def run_ring(args, rank, world, local_rank):
                 "data": "synthetic N(0,1) bf16 inputs, seeded",
                 "config": {"workload": f"B{B} H{H} S{S} D{D} causal fwd+bwd, sequence split zig-zag over {world} GPUs",
                            "parallelism": f"cp{world} (ring: NCCL send/recv of K/V and dK/dV)"},
-                "device_status": list(_lib.device_status())}), flush=True)
+                "clocks": clocks, "device_status": list(_lib.device_status())}), flush=True)
     finally:
         if world > 1:
             dist.destroy_process_group()
