@@ -207,6 +207,8 @@ def ring_backward(q, k, v, o, lse, do, state: RingState, scale: float, ops):
     for t in range(P):
         src = (r - t) % P
         kv_ids = chunk_ids(src, P)
+        # next step's K/V do not depend on this step: their transfer overlaps the blocks
+        pending_kv = state.exchange.post(kv) if t + 1 < P else None
         for xi in range(2):
             for yi in range(2):
                 kind = block_kind(my_ids[xi], kv_ids[yi])
@@ -219,13 +221,11 @@ def ring_backward(q, k, v, o, lse, do, state: RingState, scale: float, ops):
                 dkv[2 + yi] += gv.float()
         if P == 1:
             break
-        # pass K/V (for the next step) and the dK/dV accumulators (always) to rank + 1;
-        # after the last step the accumulators arrive back at the rank that owns them
-        if t + 1 < P:
-            bufs = state.exchange.post(kv + dkv)()
-            kv, dkv = bufs[:4], bufs[4:]
-        else:
-            dkv = state.exchange.post(dkv)()
+        # the dK/dV accumulators go to rank + 1 after every step; after the last step
+        # they arrive back at the rank that owns them
+        dkv = state.exchange.post(dkv)()
+        if pending_kv is not None:
+            kv = pending_kv()
     dtype = q.dtype
     return (_unchunks(dq[0].to(dtype), dq[1].to(dtype), B, H), _unchunks(dkv[0].to(dtype), dkv[1].to(dtype), B, H),
             _unchunks(dkv[2].to(dtype), dkv[3].to(dtype), B, H))
