@@ -164,7 +164,9 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     }
   } else if (warp == fwd::MMA_WARP) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (waits, descriptors and loop state are then
+    // warp-uniform) and one elected lane issues each group of MMAs and its commits.
+    {
       constexpr uint32_t IDESC_QK = idesc_bf16(128, fwd::BN, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
       const uint32_t q_addr0 = sbase + L::Q_OFF, q_addr1 = sbase + L::Q_OFF + L::TILE_BYTES;
@@ -176,17 +178,29 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         const uint64_t qd = i ? qdesc1 : qdesc0;
         const uint64_t kd = kmajor_desc(k_addr, 128, 0);
         const uint32_t d = tmem + i * 128;
-        mma_ss(d, qd, kd, IDESC_QK, 0u);
+        if (elect_one()) {
+          mma_ss(d, qd, kd, IDESC_QK, 0u);
 #pragma unroll
-        for (int ks = 1; ks < D / 16; ++ks) mma_ss_acc(d, qd + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_QK);
-        mma_commit(s_full(i));
+          for (int ks = 1; ks < D / 16; ++ks)
+            mma_ss_acc(d, qd + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_QK);
+          mma_commit(s_full(i));
+        }
+        __syncwarp();
       };
       auto issue_pv = [&](int i, uint32_t v_addr, int j) {
         const uint64_t vd = mnmajor_desc(v_addr, fwd::BN, 0);
         const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
-        mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
+        if (elect_one()) {
+          mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 1; ks < fwd::BN / 16; ++ks) mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
+          for (int ks = 1; ks < fwd::BN / 16; ++ks) mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
+        }
+        __syncwarp();
+      };
+      // commits track the MMAs of the thread that issues them: the same elected lane
+      auto commit = [&](uint32_t bar) {
+        if (elect_one()) mma_commit(bar);
+        __syncwarp();
       };
       // prologue: S_i(0)
       if (ok && n_kv > 0) {
@@ -197,7 +211,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
           const uint32_t k_addr = sbase + L::KV_OFF + s * L::TILE_BYTES;
           if (n_tiles0 > 0) issue_qk(0, k_addr);
           if (n_tiles1 > 0) issue_qk(1, k_addr);
-          mma_commit(kv_empty(s));
+          commit(kv_empty(s));
           ++it;
         }
       }
@@ -228,19 +242,19 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
           tc_fence_after();
           issue_pv(1, v_addr, j);
         }
-        mma_commit(kv_empty(sv));
+        commit(kv_empty(sv));
         if (next) {
           if (j + 1 < n_tiles1) issue_qk(1, k_addr);
-          mma_commit(kv_empty(sk));
+          commit(kv_empty(sk));
           ++it;
         }
       }
       if (ok) {
-        mma_commit(o_final(0));
-        mma_commit(o_final(1));
+        commit(o_final(0));
+        commit(o_final(1));
       }
       // every issued MMA has finished before TMEM is released
-      mma_commit(drain_bar);
+      commit(drain_bar);
       mbar_wait_drain(drain_bar, 0);
     }
     __syncwarp();

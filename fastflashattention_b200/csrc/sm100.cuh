@@ -34,6 +34,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// True in the lowest active lane of the calling warp (whatever the branch that got here).
+__device__ __forceinline__ bool first_active_lane() {
+  uint32_t lt;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+  return (__activemask() & lt) == 0u;
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -85,8 +92,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (*abort_flag) return false;
     if (globaltimer() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
-      atomicCAS(&g_status[0], 0u, site);
-      atomicAdd(&g_status[1], 1u);
+      if (first_active_lane()) {  // one record per waiting warp
+        atomicCAS(&g_status[0], 0u, site);
+        atomicAdd(&g_status[1], 1u);
+      }
       return false;
     }
   }
@@ -98,7 +107,7 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer() - t0 > kWaitLimitNs) {
-      atomicAdd(&g_status[2], 1u);
+      if (first_active_lane()) atomicAdd(&g_status[2], 1u);
       return;
     }
   }
