@@ -115,15 +115,36 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int e = 0; e < 64; ++e) v[e] = __uint_as_float(r[e >> 5][e & 31]);
 }
 
-// Write the accumulator columns [g*D/2, (g+1)*D/2) of this lane to a global bf16 row.
+// Stage the accumulator columns [g*D/2, (g+1)*D/2) of this lane (TMEM row = tile row) as
+// bf16 into a 128-row tile in shared memory laid out for a SWIZZLE_128B TMA store.
 template <int D>
-__device__ __forceinline__ void store_acc_half(uint32_t t_acc, int g, __nv_bfloat16* row, bool valid, float mul) {
+__device__ __forceinline__ void stage_acc_half(uint32_t t_acc, int g, uint32_t tile, int row, float mul) {
 #pragma unroll 1
   for (int c = g * (D / 64); c < (g + 1) * (D / 64); ++c) {
     uint32_t r[32];
     tmem_ld32(t_acc + 32 * c, r);
     tmem_ld_wait();
-    if (valid) store_row32(row + 32 * c, r, mul);
+    stage_row32_sw128(tile, row, 32 * c, r, mul);
+  }
+}
+
+// Every one of the 256 compute threads calls this, staged or not (a thread that left its
+// loop early after a timeout passes staged = false): it is a barrier for all of them.  If
+// all staged their rows, one thread stores the tiles (64-column boxes) with TMA and waits
+// for the stores to complete.  Rows at or past S are clipped by the tensor map.
+template <int D, int NT>
+__device__ __forceinline__ void store_staged(bool staged, const CUtensorMap* const (&maps)[NT], uint32_t first_tile,
+                                             int row0, int bh) {
+  fence_proxy_async_smem();
+  const bool all = named_barrier_and(1, 256, staged);
+  if (all && threadIdx.x == 0) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int sl = 0; sl < D / 64; ++sl)
+        tma_store_3d(maps[t], first_tile + t * (128 * D * 2) + sl * 16384, sl * 64, row0, bh);
+    bulk_commit_group();
+    bulk_wait_all();
   }
 }
 }  // namespace bwd
@@ -135,6 +156,7 @@ template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     ffa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                        const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                         const float* __restrict__ LSE, const float* __restrict__ DELTA,
                         __nv_bfloat16* __restrict__ DK, __nv_bfloat16* __restrict__ DV, int S, long long stride_bh,
                         long long stride_s, float scale_log2, float scale) {
@@ -452,12 +474,15 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       if (threadIdx.x == 0) FFA_BWD_TRACE(11, i);
       mbar_arrive(ds_ready);
     }
-    if (ok && nq > 0 && mbar_wait(final_bar, 0, abort_flag, kErrBwdCompute)) {
+    const bool staged = ok && nq > 0 && mbar_wait(final_bar, 0, abort_flag, kErrBwdCompute);
+    if (staged) {
+      // every MMA has finished: the Q ring is free and holds the staged dV, dK tiles
       tc_fence_after();
-      const long long row_off = static_cast<long long>(bh) * stride_bh + static_cast<long long>(kg) * stride_s;
-      bwd::store_acc_half<D>(tmem + lane_off + 256, g, DV + row_off, kg < S, 1.f);
-      bwd::store_acc_half<D>(tmem + lane_off + 384, g, DK + row_off, kg < S, scale);
+      bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::Q_OFF, row, 1.f);
+      bwd::stage_acc_half<D>(tmem + lane_off + 384, g, sbase + L::Q_OFF + L::TILE, row, scale);
     }
+    const CUtensorMap* const maps[2] = {&tm_dv, &tm_dk};
+    bwd::store_staged<D, 2>(staged, maps, sbase + L::Q_OFF, n0, bh);
   }
 
   tc_fence_before();
@@ -478,6 +503,7 @@ template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_dq,
                       const float* __restrict__ LSE, const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ DQ,
                       int S, long long stride_bh, long long stride_s, float scale_log2, float scale) {
   using L = bwd::DqLayout<D>;
@@ -717,11 +743,14 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       mbar_arrive(ds_ready);
       if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(11 + 4 * g, j);
     }
-    if (ok && nk > 0 && mbar_wait(final_bar, 0, abort_flag, kErrDqCompute)) {
+    const bool staged = ok && nk > 0 && mbar_wait(final_bar, 0, abort_flag, kErrDqCompute);
+    if (staged) {
+      // every MMA has finished: the K ring is free and holds the staged dQ tile
       tc_fence_after();
-      const long long row_off = static_cast<long long>(bh) * stride_bh + static_cast<long long>(qg) * stride_s;
-      bwd::store_acc_half<D>(tmem + lane_off + 256, g, DQ + row_off, qg < S, scale);
+      bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::K_OFF, row, scale);
     }
+    const CUtensorMap* const maps[1] = {&tm_dq};
+    bwd::store_staged<D, 1>(staged, maps, sbase + L::K_OFF, m0, bh);
   }
 
   tc_fence_before();
@@ -744,12 +773,15 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  CUtensorMap tdk, tdv;
+  if ((rc = make_tile_map(&tdk, a.dk, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  if ((rc = make_tile_map(&tdv, a.dv, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   auto kern = ffa_bwd_dkdv_kernel<D, CAUSAL>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LK::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
-  kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, a.lse, a.delta,
+  kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, tdk, tdv, a.lse, a.delta,
                                                         static_cast<__nv_bfloat16*>(a.dk),
                                                         static_cast<__nv_bfloat16*>(a.dv), a.S, a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
@@ -768,12 +800,14 @@ static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  CUtensorMap tdq;
+  if ((rc = make_tile_map(&tdq, a.dq, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   auto kern = ffa_bwd_dq_kernel<D, CAUSAL>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
-  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, a.lse, a.delta,
+  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, tdq, a.lse, a.delta,
                                                         static_cast<__nv_bfloat16*>(a.dq), a.S, a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
                                                         static_cast<float>(a.scale));

@@ -61,8 +61,8 @@ struct Layout {
 template <int D, bool CAUSAL, int EMU = fwd::EMU_PAIRS>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ O,
-                   float* __restrict__ LSE, int S, long long o_stride_bh, long long o_stride_s,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                   float* __restrict__ LSE, int S,
                    float scale_log2) {
   using L = fwd::Layout<D>;
   constexpr int SLABS = D / 64;
@@ -374,34 +374,33 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       tc_fence_before();
       mbar_arrive(p_ready(i));
     }
-    if (ok && nt > 0) {
-      ok = mbar_wait(o_final(i), 0, abort_flag, kErrFwdSoftmax);
-      if (ok) {
-        tc_fence_after();
-        const float l_safe = (l == 0.f) ? 1.f : l;
-        const float inv_l = 1.f / l_safe;
-        __nv_bfloat16* orow = O + bh * o_stride_bh + static_cast<long long>(grow) * o_stride_s;
+    // Epilogue: O_i / l into its Q tile (free once every MMA of tile i has finished), then
+    // one TMA store; rows at or past S are clipped by the tensor map.  Every thread of the
+    // warpgroup reaches the barrier, finished or not, so none can wait for one that left.
+    const bool staged = ok && nt > 0 && mbar_wait(o_final(i), 0, abort_flag, kErrFwdSoftmax);
+    const uint32_t o_tile = sbase + L::Q_OFF + i * L::TILE_BYTES;
+    if (staged) {
+      tc_fence_after();
+      const float l_safe = (l == 0.f) ? 1.f : l;
+      const float inv_l = 1.f / l_safe;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_o + c * 32, r);
-          tmem_ld_wait();
-          if (grow < S) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              packed[e] = pack_bf16x2(__uint_as_float(r[2 * e]) * inv_l, __uint_as_float(r[2 * e + 1]) * inv_l);
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              dst[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
-          }
-        }
-        if (LSE != nullptr && grow < S) {
-          const float m_fin = (m_used == -INFINITY) ? 0.f : m_used;
-          LSE[static_cast<long long>(bh) * S + grow] = m_fin + __log2f(l_safe);
-        }
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_o + c * 32, r);
+        tmem_ld_wait();
+        stage_row32_sw128(o_tile, row, 32 * c, r, inv_l);
       }
+      if (LSE != nullptr && grow < S) {
+        const float m_fin = (m_used == -INFINITY) ? 0.f : m_used;
+        LSE[static_cast<long long>(bh) * S + grow] = m_fin + __log2f(l_safe);
+      }
+    }
+    fence_proxy_async_smem();
+    if (named_barrier_and(1 + i, 128, staged) && row == 0) {
+#pragma unroll
+      for (int sl = 0; sl < SLABS; ++sl) tma_store_3d(&tm_o, o_tile + sl * 16384, sl * 64, mi, bh);
+      bulk_commit_group();
+      bulk_wait_all();
     }
   }
 
@@ -424,6 +423,8 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
+  CUtensorMap to;
+  if ((rc = make_tile_map(&to, a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   auto kern = ffa_fwd_kernel<D, CAUSAL, EMU>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
@@ -439,8 +440,7 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if (launch_regs < fwd::LAUNCH_REGS_NEEDED)
     return set_error(FFA_ERR_LAUNCH, "forward kernel compiled with too few registers for its setmaxnreg split");
   const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
-  kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(a.o), a.lse,
-                                                        a.S, a.stride_bh, a.stride_s,
+  kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, to, a.lse, a.S,
                                                         static_cast<float>(a.scale * kLog2e));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));

@@ -129,6 +129,32 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* m, 
       : "memory");
 }
 
+// TMA tile store (shared -> global) in a bulk group.  Box rows and columns outside the
+// tensor are not written, so a ragged last tile needs no masking.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Barrier among `n` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is
+// __syncthreads) that also returns whether `pred` holds in all of them.
+__device__ __forceinline__ bool named_barrier_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -140,6 +166,10 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -401,6 +431,29 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// Write 32 fp32 values (times `mul`, as bf16) of row `row`, columns [col0, col0+32), into a
+// 128-row bf16 tile staged in shared memory for a SWIZZLE_128B TMA store: 64-column
+// slabs of 16 KB, 128 bytes per row, 16-byte chunk k of a row at (k ^ (row & 7)) * 16.
+// Rows of a warp hit distinct banks for every chunk.
+__device__ __forceinline__ void stage_row32_sw128(uint32_t tile, int row, int col0, const uint32_t (&r)[32],
+                                                  float mul) {
+  const uint32_t line = tile + (col0 >> 6) * 16384 + row * 128;
+  const uint32_t x = static_cast<uint32_t>(row & 7);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t k = static_cast<uint32_t>(((col0 & 63) >> 3) + e);
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = 8 * e + 2 * u;
+      w[u] = pack_bf16x2(__uint_as_float(r[i]) * mul, __uint_as_float(r[i + 1]) * mul);
+    }
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(line + ((k ^ x) << 4)), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
 }
 
 }  // namespace ffa
