@@ -828,11 +828,54 @@ int launch_dq(const BwdArgs& a, cudaStream_t stream) {
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 
+// A second stream per device (created on first use, never destroyed) on which dQ runs
+// beside dK/dV: the two kernels are independent once delta exists, and CTAs of one fill
+// the SMs the other leaves idle at its tail.  Fork and join are event waits, so the
+// pair also records correctly into a CUDA graph captured on the caller's stream.
+// The caller holds bwd_fork_mutex() (the events are shared by every caller on a device).
+static std::mutex& bwd_fork_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
+static int side_stream(cudaStream_t* out, cudaEvent_t* fork, cudaEvent_t* join) {
+  struct Side { cudaStream_t s; cudaEvent_t f, j; };
+  static Side side[64] = {};
+  static int ready[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaGetDevice failed");
+  Side& sd = side[dev & 63];
+  {
+    if (!ready[dev & 63]) {
+      if (cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&sd.f, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&sd.j, cudaEventDisableTiming) != cudaSuccess)
+        return set_error(FFA_ERR_LAUNCH, "could not create the backward's side stream");
+      ready[dev & 63] = 1;
+    }
+  }
+  *out = sd.s;
+  *fork = sd.f;
+  *join = sd.j;
+  return FFA_OK;
+}
+
 int launch_bwd(const BwdArgs& a, cudaStream_t stream) {
   int rc;
   if ((rc = launch_preprocess(a.o, a.dout, a.delta, a.BH, a.S, a.D, a.stride_bh, a.stride_s, stream))) return rc;
+  // record / wait / launch as one unit: another thread's backward on this device must not
+  // re-record the shared events in between
+  std::lock_guard<std::mutex> lock(bwd_fork_mutex());
+  cudaStream_t side;
+  cudaEvent_t fork, join;
+  if ((rc = side_stream(&side, &fork, &join))) return rc;
+  if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "backward fork failed");
+  if ((rc = launch_dq(a, side))) return rc;
   if ((rc = launch_dkdv(a, stream))) return rc;
-  return launch_dq(a, stream);
+  if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "backward join failed");
+  return FFA_OK;
 }
 
 }  // namespace ffa

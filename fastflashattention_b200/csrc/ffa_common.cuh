@@ -3,7 +3,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/ffa.h"
 #include "sm100.cuh"
