@@ -356,8 +356,9 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
           const float x0 = x.x, x1 = x.y;
           float p0, p1;
           if ((c & 7) < EMU) {
-            p0 = exp2_fma(x0);
-            p1 = exp2_fma(x1);
+            const float2 e2 = exp2_fma2(x);
+            p0 = e2.x;
+            p1 = e2.y;
           } else {
             p0 = fast_exp2(x0);
             p1 = fast_exp2(x1);

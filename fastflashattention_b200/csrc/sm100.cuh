@@ -426,6 +426,23 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// exp2_fma on two values with packed f32x2 arithmetic (the same polynomial and rounding
+// as exp2_fma, about half the instructions per value).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kShifter = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = add2(x, make_float2(kShifter, kShifter));  // low mantissa bits of t hold round(x)
+  const float2 n = sub2(t, make_float2(kShifter, kShifter));
+  const float2 f = sub2(x, n);
+  float2 p = fma2(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                  make_float2(0.2426111251115799f, 0.2426111251115799f));
+  p = fma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 // Three-input max (sm_100 max.f32 with three sources).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
