@@ -88,6 +88,18 @@ struct DqLayout {
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
 };
 
+// Whether group g of 4 consecutive exponentials (of the 64 a thread computes per step)
+// goes to the FMA pipe instead of MUFU.EX2.  At D=128 the exponentials never bound the
+// backward and none do; at D=64 the MMAs of a step take half as long and 1 group in 4
+// moves over (FFA_BWD_EMU_D64 overrides the count at build time, for measurements).
+#ifndef FFA_BWD_EMU_D64
+#define FFA_BWD_EMU_D64 1
+#endif
+template <int D>
+__device__ __forceinline__ constexpr bool emu_group(int g) {
+  return D == 64 && (g & 3) < FFA_BWD_EMU_D64;
+}
+
 // TMEM column of the 16-deep K-step `ks` of a packed-bf16 A operand written by the two
 // warpgroups (K-steps 0-3 from warpgroup 0 at base, 4-7 from warpgroup 1 at base + 64).
 __device__ __forceinline__ uint32_t packed_kstep_col(uint32_t base, int ks) {
@@ -421,10 +433,18 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           const float2 c2 = make_float2(scale_log2, scale_log2);
           const float2 xa = fma2(make_float2(p[e], p[e + 1]), c2, make_float2(-l4.x, -l4.y));
           const float2 xb = fma2(make_float2(p[e + 2], p[e + 3]), c2, make_float2(-l4.z, -l4.w));
-          p[e + 0] = fast_exp2(xa.x);
-          p[e + 1] = fast_exp2(xa.y);
-          p[e + 2] = fast_exp2(xb.x);
-          p[e + 3] = fast_exp2(xb.y);
+          if (bwd::emu_group<D>(e >> 2)) {  // this group of 4 on the FMA pipe
+            const float2 ea = exp2_fma2(xa), eb = exp2_fma2(xb);
+            p[e + 0] = ea.x;
+            p[e + 1] = ea.y;
+            p[e + 2] = eb.x;
+            p[e + 3] = eb.y;
+          } else {
+            p[e + 0] = fast_exp2(xa.x);
+            p[e + 1] = fast_exp2(xa.y);
+            p[e + 2] = fast_exp2(xb.x);
+            p[e + 3] = fast_exp2(xb.y);
+          }
           if (need_mask) {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
@@ -727,8 +747,15 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
         const float2 x = fma2(make_float2(sv[e], sv[e + 1]), c2, l2);
-        float p0 = fast_exp2(x.x);
-        float p1 = fast_exp2(x.y);
+        float p0, p1;
+        if (bwd::emu_group<D>(e >> 2)) {  // this pair on the FMA pipe
+          const float2 ex = exp2_fma2(x);
+          p0 = ex.x;
+          p1 = ex.y;
+        } else {
+          p0 = fast_exp2(x.x);
+          p1 = fast_exp2(x.y);
+        }
         if (need_mask) {
           if (kc + e > lim) p0 = 0.f;
           if (kc + e + 1 > lim) p1 = 0.f;

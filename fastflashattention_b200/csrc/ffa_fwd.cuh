@@ -41,7 +41,12 @@ constexpr int REGS_SOFTMAX = 208;
 constexpr int REGS_CONTROL = 88;
 constexpr int LAUNCH_REGS_NEEDED = (2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL) / NTHREADS;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr int EMU_PAIRS = 0;  // of every 8 column pairs of an unmasked tile, exponentiated on the FMA pipe
+// Of every 8 column pairs of an unmasked tile, how many are exponentiated on the FMA pipe
+// (packed polynomial) instead of MUFU.EX2.  At D=128 the MMAs and exponentials of a tile
+// take about the same time and the FMA share never helped; at D=64 the MMAs take half as
+// long, the softmax bounds the kernel and 2 of 8 pairs gain 10-13 % (B200, B8 H16 D64).
+template <int D>
+constexpr int emu_pairs() { return D == 64 ? 2 : 0; }
 // (measured on B200 at B4 H16 S8192 D128 causal: 0 -> 1.12 ms, 2 -> 1.23 ms, 3 -> 1.36 ms;
 // the softmax is issue-bound, not MUFU-bound, so the FMA-pipe exp2 stays off by default)
 
@@ -58,7 +63,7 @@ struct Layout {
 };
 }  // namespace fwd
 
-template <int D, bool CAUSAL, int EMU = fwd::EMU_PAIRS>
+template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>()>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -448,12 +453,12 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   return FFA_OK;
 }
 
-// Share of exponentials taken on the FMA pipe, in column pairs out of 8.  The default is
-// fwd::EMU_PAIRS; FFA_FWD_EMU=0..4 overrides it (for measurements only).
-static int fwd_emu_setting() {
+// Share of exponentials taken on the FMA pipe, in column pairs out of 8: fwd::emu_pairs<D>()
+// unless FFA_FWD_EMU=0..4 overrides it (for measurements only).
+static int fwd_emu_override() {
   static const int v = [] {
     const char* e = std::getenv("FFA_FWD_EMU");
-    if (e == nullptr || e[0] < '0' || e[0] > '4' || e[1] != '\0') return fwd::EMU_PAIRS;
+    if (e == nullptr || e[0] < '0' || e[0] > '4' || e[1] != '\0') return -1;
     return e[0] - '0';
   }();
   return v;
@@ -461,7 +466,8 @@ static int fwd_emu_setting() {
 
 template <int D, bool CAUSAL>
 static int launch_fwd_emu(const FwdArgs& a, cudaStream_t stream) {
-  switch (fwd_emu_setting()) {
+  const int o = fwd_emu_override();
+  switch (o < 0 ? fwd::emu_pairs<D>() : o) {
     case 0: return launch_fwd_t<D, CAUSAL, 0>(a, stream);
     case 1: return launch_fwd_t<D, CAUSAL, 1>(a, stream);
     case 3: return launch_fwd_t<D, CAUSAL, 3>(a, stream);
