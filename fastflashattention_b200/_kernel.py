@@ -14,6 +14,8 @@ while the softmax scale keeps using the true head dim.
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.nn.functional as F
 from torch.autograd.function import once_differentiable
@@ -46,6 +48,13 @@ def _stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def _on_device(dev: torch.device):
+    """Context that makes `dev` current for the launch (a no-op when it already is)."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
+
+
 def fastflash_attn(q, k, v, causal: bool, return_lse: bool = False, scale=None):
     """Exact bf16 attention forward. [B,H,S,D] bf16 -> [B,H,S,D] bf16 (+ base-2 LSE [B,H,S]).
 
@@ -61,7 +70,7 @@ def fastflash_attn(q, k, v, causal: bool, return_lse: bool = False, scale=None):
     o = torch.empty_like(qf)
     lse = torch.empty(B * H, S, device=q.device, dtype=torch.float32) if return_lse else None
     sm = _default_scale(D) if scale is None else float(scale)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         rc = lib.ffa_fwd(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), o.data_ptr(),
                          lse.data_ptr() if lse is not None else None,
                          B * H, S, kd, qf.stride(0), qf.stride(1), sm, int(bool(causal)),
@@ -87,7 +96,7 @@ def _bwd(q, k, v, o, do, lse, causal: bool, scale):
     dv = torch.empty_like(vf)
     delta = torch.empty(B * H, S, device=q.device, dtype=torch.float32)
     sm = _default_scale(D) if scale is None else float(scale)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         rc = lib.ffa_bwd(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), of.data_ptr(), dof.data_ptr(),
                          lf.data_ptr(), delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                          B * H, S, kd, qf.stride(0), qf.stride(1), sm, int(bool(causal)),

@@ -51,6 +51,8 @@ class FFAError(RuntimeError):
 def load(path: Path | str | None = None) -> ctypes.CDLL:
     """Load (once) and return the library; raises if it does not exist."""
     global _lib
+    if path is None and _lib is not None:  # loaded: no lock needed
+        return _lib
     with _lock:
         if _lib is not None and path is None:
             return _lib

@@ -48,15 +48,50 @@ int set_error(int code, const char* msg) {
 // Make the current device's primary context current on the calling thread.  Callers
 // such as torch's autograd worker threads select a device without ever touching the
 // runtime, and the driver-level tensor-map encoder needs a current context.
+// Done once per thread and device (a thread that switches devices sets the new one).
 int ensure_context() {
+  static thread_local int t_ctx_dev = -1;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess)
-    return set_error(FFA_ERR_LAUNCH, "no usable CUDA device on this thread");
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "no usable CUDA device on this thread");
+  if (dev != t_ctx_dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "no usable CUDA device on this thread");
+    t_ctx_dev = dev;
+  }
   return FFA_OK;
 }
 
+// Encoded tensor maps of recent calls, per thread.  A map depends only on the fields of
+// the key (no device memory is read when encoding), so a hit returns exactly what the
+// encoder would; callers that reuse their buffers (the torch caching allocator does)
+// skip the driver call.
+namespace {
+struct MapKey {
+  const void* base;
+  int BH, S, D, box_rows;
+  long long stride_bh, stride_s;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && BH == o.BH && S == o.S && D == o.D && box_rows == o.box_rows &&
+           stride_bh == o.stride_bh && stride_s == o.stride_s;
+  }
+};
+struct MapCache {
+  static constexpr int N = 16;
+  MapKey key[N];
+  CUtensorMap map[N];
+  bool used[N] = {};
+  int next = 0;
+};
+thread_local MapCache t_maps;
+}  // namespace
+
 int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long long stride_bh,
                   long long stride_s, int box_rows) {
+  const MapKey key{base, BH, S, D, box_rows, stride_bh, stride_s};
+  for (int i = 0; i < MapCache::N; ++i)
+    if (t_maps.used[i] && t_maps.key[i] == key) {
+      *map = t_maps.map[i];
+      return FFA_OK;
+    }
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return set_error(FFA_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
@@ -71,6 +106,11 @@ int make_tile_map(CUtensorMap* map, const void* base, int BH, int S, int D, long
     std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
     return set_error(FFA_ERR_INVALID, buf);
   }
+  const int slot = t_maps.next;
+  t_maps.next = (slot + 1) % MapCache::N;
+  t_maps.key[slot] = key;
+  t_maps.map[slot] = *map;
+  t_maps.used[slot] = true;
   return FFA_OK;
 }
 
