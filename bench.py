@@ -506,6 +506,172 @@ def run_ring(args, rank, world, local_rank):
     return 0
 
 
+# ------------------------------------------------------------------ comparator sweep
+SWEEP_S = [512, 1024, 2048, 4096, 8192, 16384]
+
+
+def _comparators(causal):
+    """name -> f(q, k, v) over [B,H,S,D] bf16 tensors, for every implementation that
+    imports here.  Library kernels (cuDNN SDPA through torch, FlashAttention-2, the
+    reference's Triton kernels from baseline/_ref) run as black boxes, as in the
+    reference's bench/benchmark.py:25-41 (FA2 in [B,S,H,D] framing, transposed in and out)."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from fastflashattention_b200 import fast_attention
+
+    impls = {"ours": lambda a, b, c: fast_attention(a, b, c, is_causal=causal)}
+    notes = {}
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "fastflash_attention" / "__init__.py").exists():
+        sys.path.insert(0, str(ref_dir))
+        try:
+            import fastflash_attention as ref_mod
+            impls["reference_triton"] = lambda a, b, c: ref_mod.fast_attention(a, b, c, is_causal=causal)
+        except Exception as e:  # noqa: BLE001
+            notes["reference_triton"] = f"import failed: {e!r}"[:200]
+        finally:
+            sys.path.remove(str(ref_dir))
+    else:
+        notes["reference_triton"] = "baseline/_ref not installed"
+
+    def cudnn(a, b, c):
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            return F.scaled_dot_product_attention(a, b, c, is_causal=causal)
+    impls["cudnn_sdpa"] = cudnn
+    try:
+        from flash_attn import flash_attn_func
+
+        def fa2(a, b, c, det):
+            q2, k2, v2 = (t.transpose(1, 2).contiguous() for t in (a, b, c))
+            return flash_attn_func(q2, k2, v2, causal=causal, deterministic=det).transpose(1, 2)
+        impls["fa2"] = lambda a, b, c: fa2(a, b, c, False)
+        impls["fa2_det"] = lambda a, b, c: fa2(a, b, c, True)
+    except Exception as e:  # noqa: BLE001
+        notes["fa2"] = f"import failed: {e!r}"[:200]
+    return impls, notes
+
+
+def _event_ms(fn, warmup, iters):
+    """Median CUDA-event time of fn() in ms (warm-up excluded), like bench/common.py:78-103."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = []
+    for _ in range(iters):
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b))
+    return statistics.median(out)
+
+
+def run_sweep(args):
+    """Forward / backward / step times of every comparator over the reference's S sweep
+    (bench/benchmark.py: B4 H16, D in {64, 128}, causal and not).  One JSON line per
+    (D, causal, S); an implementation that fails at a shape reports its error instead."""
+    import torch
+    sys.path.insert(0, str(ROOT))
+    torch.cuda.set_device(0)
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks["bf16_tflops"])
+    blocks = [(128, True), (64, False), (128, False), (64, True)]
+    Ss = [int(x) for x in args.sweep_s.split(",")] if args.sweep_s else SWEEP_S
+    for D, causal in blocks:
+        impls, notes = _comparators(causal)
+        for S in Ss:
+            g = torch.Generator(device="cuda").manual_seed(0)
+            mk = lambda: torch.randn(args.B, args.H, S, D, device="cuda", dtype=torch.bfloat16, generator=g)  # noqa: E731
+            q, k, v, do = mk(), mk(), mk(), mk()
+            fwd, step = attn_flops(args.B, args.H, S, D, causal)
+            row = {"mode": "sweep", "B": args.B, "H": args.H, "S": S, "D": D, "causal": causal,
+                   "peak_tflops": peak, "peak_source": peak_kind, "impls": {}, "notes": notes}
+            for name, fn in impls.items():
+                try:
+                    with torch.no_grad():
+                        t_f = _event_ms(lambda: fn(q, k, v), args.warmup, args.steps)
+                    qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+                    out = fn(qg, kg, vg)
+                    t_b = _event_ms(lambda: torch.autograd.grad(out, (qg, kg, vg), do, retain_graph=True),
+                                    args.warmup, args.steps)
+                    del out
+
+                    def st():
+                        o_ = fn(qg, kg, vg)
+                        torch.autograd.grad(o_, (qg, kg, vg), do)
+                    t_s = _event_ms(st, args.warmup, args.steps)
+                    row["impls"][name] = {
+                        "fwd_ms": round(t_f, 4), "bwd_ms": round(t_b, 4), "step_ms": round(t_s, 4),
+                        "fwd_tflops": round(fwd / t_f / 1e9, 1), "bwd_tflops": round((step - fwd) / t_b / 1e9, 1),
+                        "step_tflops": round(step / t_s / 1e9, 1),
+                        "step_pct_measured_peak": round(100 * step / t_s / 1e9 / peak, 1)}
+                except Exception as e:  # noqa: BLE001
+                    row["impls"][name] = {"error": f"{type(e).__name__}: {e}"[:200]}
+                torch.cuda.empty_cache()
+            print(json.dumps(row), flush=True)
+            del q, k, v, do
+            torch.cuda.empty_cache()
+    return 0
+
+
+# ------------------------------------------------------------------------ peak memory
+def _mem_worker(impl, S, regime, B, H, D):
+    """Peak allocated MB of one (impl, S, regime) point in this fresh process (the
+    reference's bench/mem.py:37-75 method: warm up, gc, reset the peak, one call)."""
+    import gc
+    import torch
+    sys.path.insert(0, str(ROOT))
+    torch.cuda.set_device(0)
+    fn = _comparators(True)[0][impl]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    mk = lambda: torch.randn(B, H, S, D, device="cuda", dtype=torch.bfloat16, generator=g)  # noqa: E731
+    q, k, v, do = mk(), mk(), mk(), mk()
+    if regime == "fwd":
+        def step():
+            with torch.no_grad():
+                fn(q, k, v)
+    else:
+        def step():
+            qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+            out = fn(qg, kg, vg)
+            torch.autograd.grad(out, (qg, kg, vg), do)
+    for _ in range(6):
+        step()
+    torch.cuda.synchronize()
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    step()
+    torch.cuda.synchronize()
+    print(json.dumps({"impl": impl, "S": S, "regime": regime,
+                      "peak_mb": round(torch.cuda.max_memory_allocated() / 1e6, 1)}), flush=True)
+    return 0
+
+
+def run_mem(args):
+    """Peak allocated memory, forward-only and training step, B4 H16 D128 causal, each
+    point in a fresh process; one JSON line per S with every implementation's MB."""
+    Ss = [int(x) for x in args.sweep_s.split(",")] if args.sweep_s else SWEEP_S
+    impls = ["ours", "reference_triton", "fa2", "cudnn_sdpa"]
+    for S in Ss:
+        row = {"mode": "mem", "B": args.B, "H": args.H, "S": S, "D": 128, "causal": True,
+               "inputs_mb": round(4 * args.B * args.H * S * 128 * 2 / 1e6, 1), "fwd": {}, "train": {}}
+        for regime in ("fwd", "train"):
+            for impl in impls:
+                cp = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--mode", "mem-worker",
+                                     "--mem-impl", impl, "--S", str(S), "--mem-regime", regime,
+                                     "--B", str(args.B), "--H", str(args.H)],
+                                    capture_output=True, text=True)
+                lines = [ln for ln in cp.stdout.splitlines() if ln.startswith("{")]
+                row[regime][impl] = (json.loads(lines[-1])["peak_mb"] if lines and cp.returncode == 0
+                                     else "error: " + (cp.stderr.strip().splitlines() or ["?"])[-1][:160])
+        print(json.dumps(row), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,9 +684,14 @@ def main():
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["shard", "ring"], default="shard",
+    ap.add_argument("--mode", choices=["shard", "ring", "sweep", "mem", "mem-worker"], default="shard",
                     help="shard: batch x head data parallel (default workload); ring: context-parallel ring "
-                         "over the sequence (BASELINE configs[4]: B1 H32 S131072 D128)")
+                         "over the sequence (BASELINE configs[4]: B1 H32 S131072 D128); sweep: fwd/bwd/step "
+                         "of this library beside cuDNN SDPA, FlashAttention-2 and the reference's Triton "
+                         "kernels over S (one GPU); mem: peak memory of the same, fresh process per point")
+    ap.add_argument("--sweep-s", default="", help="comma-separated S list for --mode sweep/mem")
+    ap.add_argument("--mem-impl", default="ours")
+    ap.add_argument("--mem-regime", choices=["fwd", "train"], default="train")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -531,6 +702,12 @@ def main():
         return run_reference(args, rank, world)
     if args.mode == "ring":
         return run_ring(args, rank, world, local_rank)
+    if args.mode == "sweep":
+        return run_sweep(args)
+    if args.mode == "mem":
+        return run_mem(args)
+    if args.mode == "mem-worker":
+        return _mem_worker(args.mem_impl, args.S, args.mem_regime, args.B, args.H, args.D)
     if world > 1:
         import torch
         import torch.distributed as dist
