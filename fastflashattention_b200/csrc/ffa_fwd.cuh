@@ -19,7 +19,9 @@
 // P_i (bf16, two per column) overwrites the first 64 columns of S_i and is the
 // A operand of the P.V MMA straight from tensor memory, so P never touches smem.
 // While warpgroup 0 exponentiates tile 0, the tensor core works on tile 1 and vice
-// versa.  The running max is rescaled lazily: O and l are rescaled only when a row's
+// versa.  P is handed over in two 64-key halves: the first half's P.V MMAs run while
+// the second half is exponentiated (B200, B4 H16 S8192 D128: causal -2 %, non-causal
+// -4 %; B8 H16 S4096 D64 -4 %).  The running max is rescaled lazily: O and l are rescaled only when a row's
 // max grows by more than 2^8, which keeps every P <= 256 (exact in fp32 / bf16 range).
 #pragma once
 #include <cstdlib>
@@ -56,14 +58,17 @@ struct Layout {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
-  // barriers: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain
-  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1;
+  // barriers: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain,
+  // p_half[2]
+  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;  // + alignment slack
 };
 }  // namespace fwd
 
-template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>()>
+// SPLIT: the softmax hands P over in two halves of 64 keys (barriers p_half, then
+// p_ready), so the P.V MMAs of the first half run while the second half is exponentiated.
+template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>(), bool SPLIT = true>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -82,6 +87,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   auto p_ready = [&](int i) { return bar0 + 8 * (3 + 2 * fwd::STAGES + i); };
   auto o_final = [&](int i) { return bar0 + 8 * (5 + 2 * fwd::STAGES + i); };
   const uint32_t drain_bar = bar0 + 8 * (7 + 2 * fwd::STAGES);
+  auto p_half = [&](int i) { return bar0 + 8 * (8 + 2 * fwd::STAGES + i); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
@@ -111,6 +117,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       mbar_init(s_full(i), 1);
       mbar_init(p_ready(i), 128);
       mbar_init(o_final(i), 1);
+      mbar_init(p_half(i), 128);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -192,15 +199,31 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         }
         __syncwarp();
       };
-      auto issue_pv = [&](int i, uint32_t v_addr, int j) {
+      // K-steps [k0, k1) of O_i += P_i V_j (16 keys = 8 TMEM columns of packed P each)
+      auto issue_pv = [&](int i, uint32_t v_addr, int j, int k0, int k1) {
         const uint64_t vd = mnmajor_desc(v_addr, fwd::BN, 0);
         const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
         if (elect_one()) {
-          mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
-#pragma unroll
-          for (int ks = 1; ks < fwd::BN / 16; ++ks) mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
+          for (int ks = k0; ks < k1; ++ks) {
+            if (ks == 0)
+              mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
+            else
+              mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
+          }
         }
         __syncwarp();
+      };
+      // P_i(j) V_j: in two halves when the softmax hands P over in halves
+      auto issue_pv_tile = [&](int i, uint32_t v_addr, int j) -> bool {
+        if (SPLIT) {
+          if (!mbar_wait(p_half(i), j & 1, abort_flag, kErrFwdMma)) return false;
+          tc_fence_after();
+          issue_pv(i, v_addr, j, 0, fwd::BN / 32);
+        }
+        if (!mbar_wait(p_ready(i), j & 1, abort_flag, kErrFwdMma)) return false;
+        tc_fence_after();
+        issue_pv(i, v_addr, j, SPLIT ? fwd::BN / 32 : 0, fwd::BN / 16);
+        return true;
       };
       // commits track the MMAs of the thread that issues them: the same elected lane
       auto commit = [&](uint32_t bar) {
@@ -230,9 +253,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         uint32_t k_addr = 0;
         // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
         if (j < n_tiles0) {
-          if (!(ok = mbar_wait(p_ready(0), j & 1, abort_flag, kErrFwdMma))) break;
-          tc_fence_after();
-          issue_pv(0, v_addr, j);
+          if (!(ok = issue_pv_tile(0, v_addr, j))) break;
         }
         if (next) {
           sk = it % fwd::STAGES;
@@ -243,9 +264,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         }
         // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
         if (j < n_tiles1) {
-          if (!(ok = mbar_wait(p_ready(1), j & 1, abort_flag, kErrFwdMma))) break;
-          tc_fence_after();
-          issue_pv(1, v_addr, j);
+          if (!(ok = issue_pv_tile(1, v_addr, j))) break;
         }
         commit(kv_empty(sv));
         if (next) {
@@ -343,42 +362,49 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       }
       const float m_safe = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t p[2][32];
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      if (need_mask) {
+      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 c2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m_safe, -m_safe);
+      // Column pairs [h*32, h*32+32) -> p[h] -> TMEM columns [h*32, h*32+32) of S_i.
+      auto half = [&](const int h) {
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < fwd::BN / 2; ++c) {
-          const float p0 = fast_exp2(s[2 * c] - m_safe);
-          const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
-          sum[c & 3] += p0 + p1;
-          p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
-        }
-      } else {
-        // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
-        const float2 c2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m_safe, -m_safe);
-#pragma unroll
-        for (int c = 0; c < fwd::BN / 2; ++c) {
-          const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), c2, nm2);
-          const float x0 = x.x, x1 = x.y;
-          float p0, p1;
-          if ((c & 7) < EMU) {
-            const float2 e2 = exp2_fma2(x);
-            p0 = e2.x;
-            p1 = e2.y;
-          } else {
-            p0 = fast_exp2(x0);
-            p1 = fast_exp2(x1);
+          for (int u = 0; u < 32; ++u) {
+            const int c = h * 32 + u;
+            const float p0 = fast_exp2(s[2 * c] - m_safe);
+            const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
+            sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
+            p[h][u] = pack_bf16x2(p0, p1);
           }
-          sum[c & 3] += p0 + p1;
-          p[c >> 5][c & 31] = pack_bf16x2(p0, p1);
+        } else {
+          // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            const int c = h * 32 + u;
+            const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), c2, nm2);
+            float p0, p1;
+            if ((c & 7) < EMU) {
+              const float2 e2 = exp2_fma2(x);
+              p0 = e2.x;
+              p1 = e2.y;
+            } else {
+              p0 = fast_exp2(x.x);
+              p1 = fast_exp2(x.y);
+            }
+            sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
+            p[h][u] = pack_bf16x2(p0, p1);
+          }
         }
-      }
-      const float rowsum = (sum[0] + sum[1]) + (sum[2] + sum[3]);
-      l += rowsum;
-      tmem_st32(t_s, p[0]);
-      tmem_st32(t_s + 32, p[1]);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_ready(i));
+        tmem_st32(t_s + 32 * h, p[h]);
+        if (SPLIT || h == 1) {
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
+        }
+      };
+      half(0);
+      half(1);
+      const float2 sv = add2(sum2[0], sum2[1]);
+      l += sv.x + sv.y;
     }
     // Epilogue: O_i / l into its Q tile (free once every MMA of tile i has finished), then
     // one TMA store; rows at or past S are clipped by the tensor map.  Every thread of the
@@ -421,7 +447,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 // host launcher
 // ------------------------------------------------------------------------------------
-template <int D, bool CAUSAL, int EMU>
+template <int D, bool CAUSAL, int EMU, bool SPLIT>
 static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   using L = fwd::Layout<D>;
   CUtensorMap tq, tk, tv;
@@ -431,7 +457,7 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   CUtensorMap to;
   if ((rc = make_tile_map(&to, a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU>;
+  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU, SPLIT>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   // The setmaxnreg split assumes the kernel is launched with 168 registers per thread;
@@ -454,31 +480,43 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
 }
 
 // Share of exponentials taken on the FMA pipe, in column pairs out of 8: fwd::emu_pairs<D>()
-// unless FFA_FWD_EMU=0..4 overrides it (for measurements only).
+// unless FFA_FWD_EMU=0..2 overrides it (for measurements only).
 static int fwd_emu_override() {
   static const int v = [] {
     const char* e = std::getenv("FFA_FWD_EMU");
-    if (e == nullptr || e[0] < '0' || e[0] > '4' || e[1] != '\0') return -1;
+    if (e == nullptr || e[0] < '0' || e[0] > '2' || e[1] != '\0') return -1;
     return e[0] - '0';
   }();
   return v;
 }
 
-template <int D, bool CAUSAL>
+// FFA_FWD_SPLIT=0 hands P over whole (for measurements only).
+static bool fwd_split() {
+  static const bool v = [] {
+    const char* e = std::getenv("FFA_FWD_SPLIT");
+    return !(e != nullptr && e[0] == '0' && e[1] == '\0');
+  }();
+  return v;
+}
+
+template <int D, bool CAUSAL, bool SPLIT>
 static int launch_fwd_emu(const FwdArgs& a, cudaStream_t stream) {
   const int o = fwd_emu_override();
   switch (o < 0 ? fwd::emu_pairs<D>() : o) {
-    case 0: return launch_fwd_t<D, CAUSAL, 0>(a, stream);
-    case 1: return launch_fwd_t<D, CAUSAL, 1>(a, stream);
-    case 3: return launch_fwd_t<D, CAUSAL, 3>(a, stream);
-    case 4: return launch_fwd_t<D, CAUSAL, 4>(a, stream);
-    default: return launch_fwd_t<D, CAUSAL, 2>(a, stream);
+    case 0: return launch_fwd_t<D, CAUSAL, 0, SPLIT>(a, stream);
+    case 1: return launch_fwd_t<D, CAUSAL, 1, SPLIT>(a, stream);
+    default: return launch_fwd_t<D, CAUSAL, 2, SPLIT>(a, stream);
   }
 }
 
+template <int D, bool CAUSAL>
+static int launch_fwd_split(const FwdArgs& a, cudaStream_t stream) {
+  return fwd_split() ? launch_fwd_emu<D, CAUSAL, true>(a, stream) : launch_fwd_emu<D, CAUSAL, false>(a, stream);
+}
+
 int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_fwd_emu<128, true>(a, stream) : launch_fwd_emu<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_fwd_emu<64, true>(a, stream) : launch_fwd_emu<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_fwd_split<128, true>(a, stream) : launch_fwd_split<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_fwd_split<64, true>(a, stream) : launch_fwd_split<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 
