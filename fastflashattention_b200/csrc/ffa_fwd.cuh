@@ -49,6 +49,12 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 // long, the softmax bounds the kernel and 2 of 8 pairs gain 10-13 % (B200, B8 H16 D64).
 template <int D>
 constexpr int emu_pairs() { return D == 64 ? 2 : 0; }
+// Whether the two softmax warpgroups take turns on the exponentials.  At D=64 the MMAs
+// of a step take half as long, both warpgroups would otherwise exponentiate at the same
+// time, and taking turns is 5-6 % faster (B8 H16 S4096 D64); at D=128 it changes
+// nothing measurable and stays off.
+template <int D>
+constexpr bool seq_turns() { return D == 64; }
 // (measured on B200 at B4 H16 S8192 D128 causal: 0 -> 1.12 ms, 2 -> 1.23 ms, 3 -> 1.36 ms;
 // the softmax is issue-bound, not MUFU-bound, so the FMA-pipe exp2 stays off by default)
 
@@ -59,16 +65,36 @@ struct Layout {
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
   // barriers: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain,
-  // p_half[2]
-  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2;
+  // p_half[2], exp_done[2]
+  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;  // + alignment slack
 };
 }  // namespace fwd
 
-// SPLIT: the softmax hands P over in two halves of 64 keys (barriers p_half, then
-// p_ready), so the P.V MMAs of the first half run while the second half is exponentiated.
-template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>(), bool SPLIT = true>
+// The softmax hands P over in two halves of 64 keys (barriers p_half, then p_ready), so
+// the P.V MMAs of the first half run while the second half is exponentiated.
+// SEQ: the two softmax warpgroups take turns on the exponentials (barriers exp_done):
+// tile 1 exponentiates step j after tile 0 has, tile 0 step j+1 after tile 1 step j.
+// Max of a 128-float row: 16 independent three-input max chains of depth 4, then a
+// short tree.  (On B200 the row max takes about 400 cycles either way: the ALU pipe is
+// shared with the other tile's exponential loop, not the chain depth, sets its pace.)
+__device__ __forceinline__ float row_max128(const float (&s)[fwd::BN]) {
+  float a[16];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) a[u] = fmax3(s[u], s[16 + u], s[32 + u]);
+#pragma unroll
+  for (int u = 0; u < 16; ++u) a[u] = fmax3(a[u], s[48 + u], s[64 + u]);
+#pragma unroll
+  for (int u = 0; u < 16; ++u) a[u] = fmax3(a[u], s[80 + u], s[96 + u]);
+#pragma unroll
+  for (int u = 0; u < 16; ++u) a[u] = fmaxf(a[u], s[112 + u]);
+  const float b0 = fmax3(a[0], a[1], a[2]), b1 = fmax3(a[3], a[4], a[5]), b2 = fmax3(a[6], a[7], a[8]);
+  const float b3 = fmax3(a[9], a[10], a[11]), b4 = fmax3(a[12], a[13], a[14]);
+  return fmax3(fmax3(b0, b1, b2), fmax3(b3, b4, a[15]), b0);
+}
+
+template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>(), bool SEQ = fwd::seq_turns<D>()>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -88,6 +114,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   auto o_final = [&](int i) { return bar0 + 8 * (5 + 2 * fwd::STAGES + i); };
   const uint32_t drain_bar = bar0 + 8 * (7 + 2 * fwd::STAGES);
   auto p_half = [&](int i) { return bar0 + 8 * (8 + 2 * fwd::STAGES + i); };
+  auto exp_done = [&](int i) { return bar0 + 8 * (10 + 2 * fwd::STAGES + i); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
@@ -118,6 +145,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       mbar_init(p_ready(i), 128);
       mbar_init(o_final(i), 1);
       mbar_init(p_half(i), 128);
+      mbar_init(exp_done(i), 128);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -215,14 +243,12 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       };
       // P_i(j) V_j: in two halves when the softmax hands P over in halves
       auto issue_pv_tile = [&](int i, uint32_t v_addr, int j) -> bool {
-        if (SPLIT) {
-          if (!mbar_wait(p_half(i), j & 1, abort_flag, kErrFwdMma)) return false;
-          tc_fence_after();
-          issue_pv(i, v_addr, j, 0, fwd::BN / 32);
-        }
+        if (!mbar_wait(p_half(i), j & 1, abort_flag, kErrFwdMma)) return false;
+        tc_fence_after();
+        issue_pv(i, v_addr, j, 0, fwd::BN / 32);
         if (!mbar_wait(p_ready(i), j & 1, abort_flag, kErrFwdMma)) return false;
         tc_fence_after();
-        issue_pv(i, v_addr, j, SPLIT ? fwd::BN / 32 : 0, fwd::BN / 16);
+        issue_pv(i, v_addr, j, fwd::BN / 32, fwd::BN / 16);
         return true;
       };
       // commits track the MMAs of the thread that issues them: the same elected lane
@@ -321,19 +347,9 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         const int lim = CAUSAL ? min(S - 1, grow) : (S - 1);
 #pragma unroll
         for (int c = 0; c < fwd::BN; ++c) s[c] = (n0 + c > lim) ? -INFINITY : s[c] * scale_log2;
-        float a[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-        for (int c = 4; c < fwd::BN; c += 8)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) a[u] = fmax3(a[u], s[c + u], s[c + 4 + u]);
-        tmax = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+        tmax = row_max128(s);
       } else if (scale_log2 >= 0.f) {
-        float a[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-        for (int c = 4; c < fwd::BN; c += 8)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) a[u] = fmax3(a[u], s[c + u], s[c + 4 + u]);
-        tmax = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])) * scale_log2;
+        tmax = row_max128(s) * scale_log2;
       } else {
         float a = s[0];
 #pragma unroll
@@ -394,13 +410,20 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
             p[h][u] = pack_bf16x2(p0, p1);
           }
         }
+        if (SEQ && h == 1) mbar_arrive(exp_done(i));
         tmem_st32(t_s + 32 * h, p[h]);
-        if (SPLIT || h == 1) {
-          tmem_st_wait();
-          tc_fence_before();
-          mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
-        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
       };
+      if (SEQ) {
+        // take turns with the other warpgroup: wait for its exponentials of step j
+        // (tile 1) or j-1 (tile 0), when it has such a step
+        const int oj = i ? j : j - 1;
+        if (oj >= 0 && oj < (i ? n_tiles0 : n_tiles1) &&
+            !(ok = mbar_wait(exp_done(i ^ 1), oj & 1, abort_flag, kErrFwdSoftmax)))
+          break;
+      }
       half(0);
       half(1);
       const float2 sv = add2(sum2[0], sum2[1]);
@@ -447,7 +470,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 // host launcher
 // ------------------------------------------------------------------------------------
-template <int D, bool CAUSAL, int EMU, bool SPLIT>
+template <int D, bool CAUSAL, int EMU, bool SEQ>
 static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   using L = fwd::Layout<D>;
   CUtensorMap tq, tk, tv;
@@ -457,7 +480,7 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   CUtensorMap to;
   if ((rc = make_tile_map(&to, a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU, SPLIT>;
+  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU, SEQ>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   // The setmaxnreg split assumes the kernel is launched with 168 registers per thread;
@@ -490,33 +513,35 @@ static int fwd_emu_override() {
   return v;
 }
 
-// FFA_FWD_SPLIT=0 hands P over whole (for measurements only).
-static bool fwd_split() {
+// fwd::seq_turns<D>() unless FFA_FWD_SEQ=0/1 overrides it (for measurements only).
+template <int D>
+static bool fwd_seq() {
   static const bool v = [] {
-    const char* e = std::getenv("FFA_FWD_SPLIT");
-    return !(e != nullptr && e[0] == '0' && e[1] == '\0');
+    const char* e = std::getenv("FFA_FWD_SEQ");
+    if (e != nullptr && (e[0] == '0' || e[0] == '1') && e[1] == '\0') return e[0] == '1';
+    return fwd::seq_turns<D>();
   }();
   return v;
 }
 
-template <int D, bool CAUSAL, bool SPLIT>
+template <int D, bool CAUSAL, bool SEQ>
 static int launch_fwd_emu(const FwdArgs& a, cudaStream_t stream) {
   const int o = fwd_emu_override();
   switch (o < 0 ? fwd::emu_pairs<D>() : o) {
-    case 0: return launch_fwd_t<D, CAUSAL, 0, SPLIT>(a, stream);
-    case 1: return launch_fwd_t<D, CAUSAL, 1, SPLIT>(a, stream);
-    default: return launch_fwd_t<D, CAUSAL, 2, SPLIT>(a, stream);
+    case 0: return launch_fwd_t<D, CAUSAL, 0, SEQ>(a, stream);
+    case 1: return launch_fwd_t<D, CAUSAL, 1, SEQ>(a, stream);
+    default: return launch_fwd_t<D, CAUSAL, 2, SEQ>(a, stream);
   }
 }
 
 template <int D, bool CAUSAL>
-static int launch_fwd_split(const FwdArgs& a, cudaStream_t stream) {
-  return fwd_split() ? launch_fwd_emu<D, CAUSAL, true>(a, stream) : launch_fwd_emu<D, CAUSAL, false>(a, stream);
+static int launch_fwd_seq(const FwdArgs& a, cudaStream_t stream) {
+  return fwd_seq<D>() ? launch_fwd_emu<D, CAUSAL, true>(a, stream) : launch_fwd_emu<D, CAUSAL, false>(a, stream);
 }
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_fwd_split<128, true>(a, stream) : launch_fwd_split<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_fwd_split<64, true>(a, stream) : launch_fwd_split<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_fwd_seq<128, true>(a, stream) : launch_fwd_seq<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_fwd_seq<64, true>(a, stream) : launch_fwd_seq<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 
