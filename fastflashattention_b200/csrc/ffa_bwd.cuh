@@ -170,8 +170,8 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                         const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                         const float* __restrict__ LSE, const float* __restrict__ DELTA,
-                        __nv_bfloat16* __restrict__ DK, __nv_bfloat16* __restrict__ DV, int S, long long stride_bh,
-                        long long stride_s, float scale_log2, float scale) {
+                        __nv_bfloat16* __restrict__ DK, __nv_bfloat16* __restrict__ DV, int S, int BH, int group,
+                        long long stride_bh, long long stride_s, float scale_log2, float scale) {
   using L = bwd::DkdvLayout<D>;
   constexpr int SLABS = D / 64;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -205,8 +205,10 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kblk = static_cast<int>(blockIdx.x);  // causal: low key blocks carry the most work and run first
-  const int bh = blockIdx.y;
+  // causal: low key blocks carry the most work and run first
+  const CtaWork work = cta_work((S + bwd::LANES - 1) / bwd::LANES, BH, group);
+  const int kblk = work.rank;
+  const int bh = work.bh;
   const int n0 = kblk * bwd::LANES;
   const int q_begin = CAUSAL ? n0 : 0;  // first query that can see a key of this block
   const int nq = (S > q_begin) ? (S - q_begin + bwd::STEP - 1) / bwd::STEP : 0;
@@ -525,7 +527,8 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_dq,
                       const float* __restrict__ LSE, const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ DQ,
-                      int S, long long stride_bh, long long stride_s, float scale_log2, float scale) {
+                      int S, int BH, int group, long long stride_bh, long long stride_s, float scale_log2,
+                      float scale) {
   using L = bwd::DqLayout<D>;
   constexpr int SLABS = D / 64;
   extern __shared__ uint8_t smem_raw[];
@@ -549,9 +552,10 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nblk = gridDim.x;
-  const int qblk = CAUSAL ? (nblk - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y;
+  const int nblk = (S + bwd::LANES - 1) / bwd::LANES;
+  const CtaWork work = cta_work(nblk, BH, group);
+  const int qblk = CAUSAL ? (nblk - 1 - work.rank) : work.rank;
+  const int bh = work.bh;
   const int m0 = qblk * bwd::LANES;
   const int nk_all = (S + bwd::STEP - 1) / bwd::STEP;
   const int nk = CAUSAL ? min(nk_all, m0 / bwd::STEP + 1) : nk_all;
@@ -807,10 +811,11 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LK::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
-  const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
+  const dim3 grid(static_cast<unsigned>((a.S + bwd::LANES - 1) / bwd::LANES) * static_cast<unsigned>(a.BH));
   kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, tdk, tdv, a.lse, a.delta,
                                                         static_cast<__nv_bfloat16*>(a.dk),
-                                                        static_cast<__nv_bfloat16*>(a.dv), a.S, a.stride_bh,
+                                                        static_cast<__nv_bfloat16*>(a.dv), a.S, a.BH,
+                                                        work_group(a.BH, a.S, D, CAUSAL), a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
                                                         static_cast<float>(a.scale));
   const cudaError_t e = cudaGetLastError();
@@ -833,9 +838,10 @@ static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
-  const dim3 grid((a.S + bwd::LANES - 1) / bwd::LANES, a.BH);
+  const dim3 grid(static_cast<unsigned>((a.S + bwd::LANES - 1) / bwd::LANES) * static_cast<unsigned>(a.BH));
   kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, tdq, a.lse, a.delta,
-                                                        static_cast<__nv_bfloat16*>(a.dq), a.S, a.stride_bh,
+                                                        static_cast<__nv_bfloat16*>(a.dq), a.S, a.BH,
+                                                        work_group(a.BH, a.S, D, CAUSAL), a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
                                                         static_cast<float>(a.scale));
   const cudaError_t e = cudaGetLastError();

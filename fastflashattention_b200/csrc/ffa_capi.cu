@@ -177,6 +177,9 @@ static int check_common(int BH, int S, int D, long long stride_bh, long long str
   if (stride_s < D || stride_s % 8 != 0) return set_error(FFA_ERR_INVALID, "stride_s must be >= D and a multiple of 8");
   if (BH > 1 && (stride_bh < static_cast<long long>(S) * stride_s || stride_bh % 8 != 0))
     return set_error(FFA_ERR_INVALID, "stride_bh must be >= S*stride_s and a multiple of 8");
+  // the kernels run one CTA per 128-row block of every slice in a 1-D grid
+  if (static_cast<long long>((S + 127) / 128) * BH > 2147483647LL)
+    return set_error(FFA_ERR_UNSUPPORTED, "BH * ceil(S/128) exceeds the grid limit of 2^31-1 CTAs");
   return FFA_OK;
 }
 

@@ -98,7 +98,7 @@ template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>(), bool SEQ = fwd::seq
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                   float* __restrict__ LSE, int S,
+                   float* __restrict__ LSE, int S, int BH, int group,
                    float scale_log2) {
   using L = fwd::Layout<D>;
   constexpr int SLABS = D / 64;
@@ -120,10 +120,11 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_mblk = gridDim.x;
+  const int n_mblk = (S + 2 * fwd::BM - 1) / (2 * fwd::BM);
+  const CtaWork work = cta_work(n_mblk, BH, group);
   // heaviest causal blocks first
-  const int mblk = CAUSAL ? (n_mblk - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y;
+  const int mblk = CAUSAL ? (n_mblk - 1 - work.rank) : work.rank;
+  const int bh = work.bh;
   const int m0 = mblk * 2 * fwd::BM;
   const int n_kv_all = (S + fwd::BN - 1) / fwd::BN;
   // number of key tiles each 128-row query tile visits (0 for a tile past the end)
@@ -494,8 +495,9 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   }
   if (launch_regs < fwd::LAUNCH_REGS_NEEDED)
     return set_error(FFA_ERR_LAUNCH, "forward kernel compiled with too few registers for its setmaxnreg split");
-  const dim3 grid((a.S + 2 * fwd::BM - 1) / (2 * fwd::BM), a.BH);
-  kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, to, a.lse, a.S,
+  const int n_mblk = (a.S + 2 * fwd::BM - 1) / (2 * fwd::BM);
+  const dim3 grid(static_cast<unsigned>(n_mblk) * static_cast<unsigned>(a.BH));
+  kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, to, a.lse, a.S, a.BH, work_group(a.BH, a.S, D, CAUSAL),
                                                         static_cast<float>(a.scale * kLog2e));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
