@@ -143,7 +143,7 @@ __device__ __forceinline__ void stage_acc_half(uint32_t t_acc, int g, uint32_t t
 // Every one of the 256 compute threads calls this, staged or not (a thread that left its
 // loop early after a timeout passes staged = false): it is a barrier for all of them.  If
 // all staged their rows, one thread stores the tiles (64-column boxes) with TMA and waits
-// for the stores to complete.  Rows at or past S are clipped by the tensor map.
+// for the stores to finish reading shared memory.  Rows at or past S are clipped by the tensor map.
 template <int D, int NT>
 __device__ __forceinline__ void store_staged(bool staged, const CUtensorMap* const (&maps)[NT], uint32_t first_tile,
                                              int row0, int bh) {
@@ -156,7 +156,7 @@ __device__ __forceinline__ void store_staged(bool staged, const CUtensorMap* con
       for (int sl = 0; sl < D / 64; ++sl)
         tma_store_3d(maps[t], first_tile + t * (128 * D * 2) + sl * 16384, sl * 64, row0, bh);
     bulk_commit_group();
-    bulk_wait_all();
+    bulk_wait_read();
   }
 }
 }  // namespace bwd

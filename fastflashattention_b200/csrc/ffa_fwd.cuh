@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 #pragma unroll
       for (int sl = 0; sl < SLABS; ++sl) tma_store_3d(&tm_o, o_tile + sl * 16384, sl * 64, mi, bh);
       bulk_commit_group();
-      bulk_wait_all();
+      bulk_wait_read();
     }
   }
 

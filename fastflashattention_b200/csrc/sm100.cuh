@@ -140,6 +140,10 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src,
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has finished reading its shared
+// memory source.  Enough before a CTA exits: the global writes still complete before the
+// kernel does (stream order), and the CTA no longer waits for their round trip.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Barrier among `n` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is
 // __syncthreads) that also returns whether `pred` holds in all of them.
 __device__ __forceinline__ bool named_barrier_and(int id, int n, bool pred) {
