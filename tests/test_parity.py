@@ -166,6 +166,42 @@ def test_forward_peaky_rows_lse_path():
         assert _rel_l2(out, _ref(q, k, v, causal, None)) < TOL
 
 
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("is_causal", [False, True])
+@pytest.mark.parametrize("boost", [(128, 192), (192, 256), (320, 384)], ids=["tile1-first-half",
+                                                                            "tile1-second-half",
+                                                                            "tile2-second-half"])
+@pytest.mark.parametrize("scale", [None, -0.09])
+def test_late_max_growth(D, is_causal, boost, scale):
+    """Scores that jump by far more than 2^8 inside a later 128-key tile, in its first or
+    second 64-key half (keys boosted x8).  This drives the forward's lazy rescale through
+    both of its late paths: the row max taken before the first half is handed over, and
+    the rescale of O after the first half's P.V has already run.  A negative scale turns
+    the max into a min."""
+    torch.manual_seed(5)
+    B, H, S = 1, 2, 512
+    q, k, v = (torch.randn(B, H, S, D, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    k[:, :, boost[0]:boost[1]] *= 8
+    q, k, v = (t.requires_grad_(True) for t in (q, k, v))
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    out = fast_attention(q, k, v, is_causal=is_causal, scale=scale)
+    ref = _ref(qr, kr, vr, is_causal, scale)
+    assert _rel_l2(out, ref) < TOL
+    _, lse = fastflash_attn(q.detach(), k.detach(), v.detach(), is_causal, return_lse=True, scale=scale)
+    sc = (1.0 / math.sqrt(D)) if scale is None else scale
+    logits = (qr.detach().double() @ kr.detach().double().transpose(-1, -2)) * sc
+    if is_causal:
+        logits = logits.masked_fill(torch.ones(S, S, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    lse_true = torch.logsumexp(logits, dim=-1) / math.log(2.0)
+    assert float((lse.double() - lse_true).abs().max()) < 2e-3
+    torch.manual_seed(6)
+    g = torch.randn_like(out)
+    out.backward(g)
+    ref.backward(g.float())
+    for name, got, want in (("dq", q.grad, qr.grad), ("dk", k.grad, kr.grad), ("dv", v.grad, vr.grad)):
+        assert _rel_l2(got, want) < TOL_PEAKY_GRAD, name
+
 @pytest.mark.parametrize("D", [1, 2, 4, 8, 16, 32])
 def test_small_head_dims_padded(D):
     torch.manual_seed(4)
