@@ -89,15 +89,17 @@ struct DqLayout {
 };
 
 // Whether group g of 4 consecutive exponentials (of the 64 a thread computes per step)
-// goes to the FMA pipe instead of MUFU.EX2.  At D=128 the exponentials never bound the
-// backward and none do; at D=64 the MMAs of a step take half as long and 1 group in 4
-// moves over (FFA_BWD_EMU_D64 overrides the count at build time, for measurements).
+// goes to the FMA pipe instead of MUFU.EX2.  At D=64 the MMAs of a step take half as long
+// and 1 group in 4 moves over in both kernels (FFA_BWD_EMU_D64 overrides the count at
+// build time, for measurements).  At D=128, 1 group in 4 in the dK/dV kernel measured
+// 2.7-3 % faster at B4 H16 causal S=512..8192, while the dQ kernel was 1.5 % slower with
+// it and keeps every exponential on MUFU.
 #ifndef FFA_BWD_EMU_D64
 #define FFA_BWD_EMU_D64 1
 #endif
-template <int D>
+template <int D, bool DKDV>
 __device__ __forceinline__ constexpr bool emu_group(int g) {
-  return D == 64 && (g & 3) < FFA_BWD_EMU_D64;
+  return (g & 3) < (D == 64 ? FFA_BWD_EMU_D64 : (DKDV ? 1 : 0));
 }
 
 // TMEM column of the 16-deep K-step `ks` of a packed-bf16 A operand written by the two
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           const float2 c2 = make_float2(scale_log2, scale_log2);
           const float2 xa = fma2(make_float2(p[e], p[e + 1]), c2, make_float2(-l4.x, -l4.y));
           const float2 xb = fma2(make_float2(p[e + 2], p[e + 3]), c2, make_float2(-l4.z, -l4.w));
-          if (bwd::emu_group<D>(e >> 2)) {  // this group of 4 on the FMA pipe
+          if (bwd::emu_group<D, true>(e >> 2)) {  // this group of 4 on the FMA pipe
             const float2 ea = exp2_fma2(xa), eb = exp2_fma2(xb);
             p[e + 0] = ea.x;
             p[e + 1] = ea.y;
@@ -752,7 +754,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       for (int e = 0; e < 64; e += 2) {
         const float2 x = fma2(make_float2(sv[e], sv[e + 1]), c2, l2);
         float p0, p1;
-        if (bwd::emu_group<D>(e >> 2)) {  // this pair on the FMA pipe
+        if (bwd::emu_group<D, false>(e >> 2)) {  // this pair on the FMA pipe
           const float2 ex = exp2_fma2(x);
           p0 = ex.x;
           p1 = ex.y;
