@@ -579,6 +579,8 @@ def run_sweep(args):
     peaks, peak_kind = load_peaks()
     peak = float(peaks["bf16_tflops"])
     blocks = [(128, True), (64, False), (128, False), (64, True)]
+    if args.sweep_blocks:  # e.g. "128c,64n": head dim, then c(ausal) or n(on-causal)
+        blocks = [(int(b[:-1]), b[-1] == "c") for b in args.sweep_blocks.split(",")]
     Ss = [int(x) for x in args.sweep_s.split(",")] if args.sweep_s else SWEEP_S
     for D, causal in blocks:
         impls, notes = _comparators(causal)
@@ -690,6 +692,7 @@ def main():
                          "of this library beside cuDNN SDPA, FlashAttention-2 and the reference's Triton "
                          "kernels over S (one GPU); mem: peak memory of the same, fresh process per point")
     ap.add_argument("--sweep-s", default="", help="comma-separated S list for --mode sweep/mem")
+    ap.add_argument("--sweep-blocks", default="", help="--mode sweep blocks, e.g. 128c,64n (default: all four)")
     ap.add_argument("--mem-impl", default="ours")
     ap.add_argument("--mem-regime", choices=["fwd", "train"], default="train")
     args = ap.parse_args()
