@@ -18,8 +18,9 @@
 // tensor core can be fed at full rate).
 //   warps 0-7  two compute warpgroups; warpgroup g handles columns [64g, 64g+64) of
 //              every step (thread = TMEM lane = one key / query row)
-//   warp  8    producer: TMA for the streamed tiles (and lse/delta for dkdv)
-//   warp  9    MMA issuer (one thread)
+//   warp  8    producer: TMA for the streamed tiles (dkdv: Q; warp 10 streams dO with
+//              lse/delta beside it)
+//   warp  9    MMA issuer (the whole warp runs the loop, an elected lane issues)
 // P and dS are written back to tensor memory as packed bf16 and feed the gradient MMAs
 // from there.  In the dq kernel dS overwrites the S columns it came from (warpgroup g's
 // 64 values land in [64g, 64g+32)).  In the dkdv kernel P and dS both go into the dP
@@ -29,7 +30,8 @@
 #pragma once
 #include "ffa_common.cuh"
 
-// Timeline hook for measurement builds (see ffa_fwd.cuh); nothing in the library.
+// Timeline hook for measurement builds (clock64 at fixed points of one CTA); expands to
+// nothing in the library.
 #ifndef FFA_BWD_TRACE
 #define FFA_BWD_TRACE(site, step)
 #endif

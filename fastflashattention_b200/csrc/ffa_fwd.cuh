@@ -12,7 +12,8 @@
 //   warps 0-3   softmax warpgroup for tile 0 (thread t owns row t: TMEM lane t)
 //   warps 4-7   softmax warpgroup for tile 1
 //   warp  8     TMA producer: Q0/Q1 once, then K_j, V_j through a 3-slot smem ring
-//   warp  9     MMA issuer (one thread): S_i = Q_i K_j^T  and  O_i += P_i V_j
+//   warp  9     MMA issuer (the whole warp runs the loop, an elected lane issues):
+//               S_i = Q_i K_j^T  and  O_i += P_i V_j
 //   warps 10-11 idle (complete the third warpgroup, which hands its registers to the
 //               softmax warpgroups with setmaxnreg: 208 vs 88 registers per thread)
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,384)  O1 [384,512).
@@ -21,8 +22,9 @@
 // While warpgroup 0 exponentiates tile 0, the tensor core works on tile 1 and vice
 // versa.  P is handed over in two 64-key halves: the first half's P.V MMAs run while
 // the second half is exponentiated (B200, B4 H16 S8192 D128: causal -2 %, non-causal
-// -4 %; B8 H16 S4096 D64 -4 %).  The running max is rescaled lazily: O and l are rescaled only when a row's
-// max grows by more than 2^8, which keeps every P <= 256 (exact in fp32 / bf16 range).
+// -4 %; B8 H16 S4096 D64 -4 %).  The running max is rescaled lazily: O and l are
+// rescaled only when a row's max grows by more than 2^8, which keeps every P <= 256
+// (exact in fp32 / bf16 range).  CTAs run in longest-job-first order (cta_work).
 #pragma once
 #include <cstdlib>
 
