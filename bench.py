@@ -359,7 +359,7 @@ def run_ours(args, rank, world, local_rank):
         hq, hk, hv, hdo = (flat(t).cpu().pin_memory() for t in (q, k, v, do))
         gq, gk, gv = (torch.empty(hq.shape, dtype=q.dtype, pin_memory=True) for _ in range(3))
         dq_in, dk_in, dv_in, ddo = (torch.empty((1, BHn, S, D), device=dev, dtype=q.dtype) for _ in range(4))
-        n_chunks = min(4, BHn)
+        n_chunks = max(1, min(args.e2e_chunks, BHn))
         bounds = [BHn * c // n_chunks for c in range(n_chunks + 1)]
         streams = [torch.cuda.Stream(device=dev) for _ in range(n_chunks)]
 
@@ -685,6 +685,7 @@ def main():
     ap.add_argument("--S", type=int, default=8192)
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks (streams) of the pipelined e2e step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["shard", "ring", "sweep", "mem", "mem-worker"], default="shard",
                     help="shard: batch x head data parallel (default workload); ring: context-parallel ring "
