@@ -46,19 +46,18 @@ constexpr int REGS_CONTROL = 88;
 constexpr int LAUNCH_REGS_NEEDED = (2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL) / NTHREADS;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 // Of every 8 column pairs of an unmasked tile, how many are exponentiated on the FMA pipe
-// (packed polynomial) instead of MUFU.EX2.  At D=128 the MMAs and exponentials of a tile
-// take about the same time and the FMA share never helped; at D=64 the MMAs take half as
-// long, the softmax bounds the kernel and 2 of 8 pairs gain 10-13 % (B200, B8 H16 D64).
+// (packed polynomial) instead of MUFU.EX2.  At D=64 the MMAs take half as long, the
+// softmax bounds the kernel and 2 of 8 pairs gain 10-13 % (B200, B8 H16 D64).  At D=128,
+// with P handed over in halves, 1 of 8 pairs gains 1.1-1.6 % at B4 H16 causal S=8192 and
+// 16384 (three interleaved A/B runs); more pairs were slower.
 template <int D>
-constexpr int emu_pairs() { return D == 64 ? 2 : 0; }
+constexpr int emu_pairs() { return D == 64 ? 2 : 1; }
 // Whether the two softmax warpgroups take turns on the exponentials.  At D=64 the MMAs
 // of a step take half as long, both warpgroups would otherwise exponentiate at the same
 // time, and taking turns is 5-6 % faster (B8 H16 S4096 D64); at D=128 it changes
 // nothing measurable and stays off.
 template <int D>
 constexpr bool seq_turns() { return D == 64; }
-// (measured on B200 at B4 H16 S8192 D128 causal: 0 -> 1.12 ms, 2 -> 1.23 ms, 3 -> 1.36 ms;
-// the softmax is issue-bound, not MUFU-bound, so the FMA-pipe exp2 stays off by default)
 
 template <int D>
 struct Layout {
