@@ -39,7 +39,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch of the dK/dV kernel, from the ncu capture
 # summarised in profiles/kernels_b2h16s8192d128_causal.md (B2 H16 = 32 slices), scaled to the
 # bench's (batch, head) slice count.
-DKDV_DRAM_BYTES_PER_SLICE = (283.553536e6 + 106.710784e6) / 32
+DKDV_DRAM_BYTES_PER_SLICE = (284.761088e6 + 109.198592e6) / 32
 
 
 def attn_flops(B, H, S, D, causal):
