@@ -69,13 +69,15 @@ struct CtaWork {
   int rank;
   int bh;
 };
-__device__ __forceinline__ CtaWork cta_work(int nblk, int BH, int group) {
-  const int L = static_cast<int>(blockIdx.x);
+__host__ __device__ __forceinline__ CtaWork cta_work_at(int L, int nblk, int BH, int group) {
   const int per_group = group * nblk;
   const int g = L / per_group;
   const int w = L - g * per_group;
-  const int gsize = min(group, BH - g * group);
+  const int gsize = (group < BH - g * group) ? group : BH - g * group;
   return {w / gsize, g * group + w % gsize};
+}
+__device__ __forceinline__ CtaWork cta_work(int nblk, int BH, int group) {
+  return cta_work_at(static_cast<int>(blockIdx.x), nblk, BH, group);
 }
 
 // Slices per work group for kernels that stream two [S, D] bf16 operands per slice.
