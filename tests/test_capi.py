@@ -53,6 +53,10 @@ def test_invalid_arguments_rejected_before_launch():
     assert lib.ffa_bwd(16, 16, 16, 16, 16, 16, 16, 16, 16, 16, 1, 64, 48, 64 * 48, 48, 0.1, 0, None) \
         == _lib.FFA_ERR_UNSUPPORTED
     assert lib.ffa_lse_merge(16, 16, 16, 16, 4, 130, 0, None) == _lib.FFA_ERR_INVALID
+    # one CTA per 128-row block of every slice in a 1-D grid: at most 2^31-1 CTAs
+    assert lib.ffa_fwd(16, 16, 16, 16, None, 1 << 30, 1024, 64, 1024 * 64, 64, 0.1, 1, None) \
+        == _lib.FFA_ERR_UNSUPPORTED
+    assert "grid" in _lib.last_error()
 
 
 def test_empty_problems_are_noops():
