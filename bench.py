@@ -9,9 +9,12 @@ of the reference's headline shape B=4, H=16, S=8192, D=128, causal (BASELINE con
 the other configs are parity-test cases).  FLOPs follow the reference convention
 (bench/common.py:142-153): fwd = 4*B*H*S^2*D*(1/2 if causal), step = 3.5 * fwd.
 
-Multi-GPU (torchrun, one process per GPU): every rank owns a disjoint batch x head slice
-of a global batch of 4*N sequences (weak scaling, no data-path collective); the time is
-the max over ranks of the device-timed region.  Rank 0 prints one JSON line.
+Multi-GPU (torchrun, one process per GPU): every rank draws the same global batch of
+4*N sequences from one seed and owns a disjoint, contiguous block of its (batch, head)
+slices (``shard.shard_heads``; weak scaling, no data-path collective); the time is the max
+over ranks of the device-timed region.  Beside it, ``configs3_box`` times BASELINE
+configs[3] as stated: one global B8 H32 S8192 D128 problem split over the N ranks
+(strong scaling).  Rank 0 prints one JSON line.
 
 ``--impl reference`` times the reference's CPU path for this hot path — its parity
 oracle, fp32 ``F.scaled_dot_product_attention`` forward + autograd backward
@@ -36,9 +39,9 @@ METRIC = "fwd+bwd attention TFLOP/s (causal, D=128) and % of B200 bf16 tensor pe
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes (read + write) per launch of the dK/dV kernel, from the ncu capture
-# summarised in profiles/kernels_b2h16s8192d128_causal.md (B2 H16 = 32 slices), scaled to the
-# bench's (batch, head) slice count.
+# DRAM bytes (read + write) per launch of the dK/dV kernel, from one ncu capture of that
+# kernel at B2 H16 S8192 D128 causal (32 slices; dram__bytes_read.sum + dram__bytes_write.sum),
+# scaled to the bench's (batch, head) slice count: traffic grows in proportion to slices.
 DKDV_DRAM_BYTES_PER_SLICE = (284.761088e6 + 109.198592e6) / 32
 
 
@@ -217,14 +220,16 @@ def run_reference(args, rank, world):
     sample = f"one (batch, head) slice of B{B} H{H} S{S} D{D} causal per step (1/{B * H} of the workload)"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t * 1e3 * B * H, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) bf16 inputs, seeded",
         "impl": "reference",
-        "config": config_dict(args, world),
+        "config": dict(config_dict(args, world),
+                       workload=f"B{B} H{H} S{S} D{D} causal fwd+bwd, sampled: each timed step is one (batch, head) "
+                                f"slice, 1/{B * H} of the workload; the rate is FLOP of that slice / its time"),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "fp32 F.scaled_dot_product_attention (math) fwd + autograd bwd on host cores: the reference's "
-                "parity oracle (tests/test_parity.py:32-35); ms_per_step extrapolated to the full batch",
+                "parity oracle (tests/test_parity.py:32-35); ms_per_step is the measured time of one sampled slice",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -232,7 +237,8 @@ def run_reference(args, rank, world):
 
 def config_dict(args, world):
     return {
-        "workload": f"B{args.B} H{args.H} S{args.S} D{args.D} causal fwd+bwd per GPU (weak scaling: global B={args.B * world})",
+        "workload": f"B{args.B} H{args.H} S{args.S} D{args.D} causal fwd+bwd per GPU (weak scaling: one global "
+                    f"problem of B={args.B * world} from one seed, each rank a contiguous block of its slices)",
         "B": args.B, "H": args.H, "S": args.S, "D": args.D, "causal": True,
         "global_batch": args.B * world, "seq_len": args.S,
         "parallelism": f"dp{world} (disjoint batch x head slices, no collective)",
@@ -248,23 +254,51 @@ def run_ours(args, rank, world, local_rank):
     from fastflashattention_b200 import _lib, fast_attention
     from fastflashattention_b200._kernel import fastflash_attn
 
+    from fastflashattention_b200 import shard
+
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     B, H, S, D = args.B, args.H, args.S, args.D
     causal = True
     fwd_flops, step_flops = attn_flops(B, H, S, D, causal)
-    gen = torch.Generator(device=dev).manual_seed(1000 * rank)
-    mk = lambda: torch.randn(B, H, S, D, device=dev, dtype=torch.bfloat16, generator=gen)  # noqa: E731
-    q, k, v, do = mk(), mk(), mk(), mk()
-    qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
-
-    def step():
-        o = fast_attention(qg, kg, vg, is_causal=causal)
-        return torch.autograd.grad(o, (qg, kg, vg), do)
 
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def global_inputs(Bg, Hg, seed):
+        """One global problem [Bg, Hg, S, D] drawn from one seed (every rank draws the same
+        tensors) and this rank's contiguous block of (batch, head) slices of it, as views
+        (shard.shard_heads); the global tensors are kept alive by the views."""
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        full = [torch.randn(Bg, Hg, S, D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(4)]
+        return [shard.shard_heads(t, rank, world) for t in full]
+
+    def make_step(q_, k_, v_, do_):
+        qg_, kg_, vg_ = (t.detach().requires_grad_(True) for t in (q_, k_, v_))
+
+        def step():
+            o = fast_attention(qg_, kg_, vg_, is_causal=causal)
+            return torch.autograd.grad(o, (qg_, kg_, vg_), do_)
+        return step
+
+    def timed(step, n):
+        """Device ms per step over `n` steps on this rank, then the max over ranks."""
+        e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0_.record(torch.cuda.current_stream(dev))
+        for _ in range(n):
+            step()
+        e1_.record(torch.cuda.current_stream(dev))
+        torch.cuda.synchronize()
+        barrier()
+        return shard.max_over_ranks(e0_.elapsed_time(e1_) / n)
+
+    # Weak scaling (the headline line): a global batch of B*world sequences, H heads, one
+    # seed; every rank owns B*H slices of it (world == 1: the whole B x H problem).
+    q, k, v, do = (t.reshape(B, H, S, D) for t in global_inputs(B * world, H, 0))
+    step = make_step(q, k, v, do)
 
     for _ in range(args.warmup):
         step()
@@ -287,12 +321,26 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop()
-    ms = ms_local
-    if world > 1:
-        t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shard.max_over_ranks(ms_local)
     value = world * step_flops / (ms / 1e3) / 1e12
+
+    # BASELINE configs[3] as stated: ONE global B8 H32 S8192 D128 causal problem split over
+    # the ranks (strong scaling, whole-box TFLOP/s = total FLOP / max-rank time).
+    box = None
+    if not args.no_box:
+        Bb, Hb = 8, 32
+        bq, bk, bv, bdo = global_inputs(Bb, Hb, 3)
+        bstep = make_step(bq, bk, bv, bdo)
+        for _ in range(args.warmup):
+            bstep()
+        bms = timed(bstep, max(3, args.steps // 2))
+        _, box_flops = attn_flops(Bb, Hb, S, D, causal)
+        box = {"workload": f"B{Bb} H{Hb} S{S} D{D} causal fwd+bwd, one global problem split over {world} GPU(s) "
+                           f"({bq.shape[1]} of {Bb * Hb} (batch, head) slices on rank 0)",
+               "value": box_flops / (bms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": bms, "scaling": "strong",
+               "parallelism": f"dp{world} (shard.shard_heads of one global tensor, no collective)"}
+        del bq, bk, bv, bdo, bstep
+        torch.cuda.empty_cache()
 
     # ---- per-kernel times (same inputs, each kernel alone, CUDA events on this stream)
     lib = _lib.load()
@@ -425,6 +473,7 @@ def run_ours(args, rank, world, local_rank):
                          "of_spec_2250": round(100 * value / world / spec, 2)},
             "roofline": roofline,
             "kernels": kinfo,
+            "configs3_box": box,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
@@ -687,6 +736,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks (streams) of the pipelined e2e step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-box", action="store_true", help="skip the B8 H32 global-problem (configs[3]) figure")
     ap.add_argument("--mode", choices=["shard", "ring", "sweep", "mem", "mem-worker"], default="shard",
                     help="shard: batch x head data parallel (default workload); ring: context-parallel ring "
                          "over the sequence (BASELINE configs[4]: B1 H32 S131072 D128); sweep: fwd/bwd/step "

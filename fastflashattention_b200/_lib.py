@@ -25,11 +25,14 @@ _D = ctypes.c_double
 _FP = ctypes.POINTER(ctypes.c_float)
 SIGNATURES = {
     "ffa_fwd": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
+    "ffa_fwd_merge": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _I, _VP]),
     "ffa_bwd_preprocess": (_I, [_VP, _VP, _VP, _I, _I, _I, _LL, _LL, _VP]),
     "ffa_bwd": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_noalloc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_dkdv": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_bwd_dq": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
+    "ffa_bwd_dkdv_acc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
+    "ffa_bwd_dq_acc": (_I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL, _D, _I, _VP]),
     "ffa_lse_merge": (_I, [_VP, _VP, _VP, _VP, _LL, _I, _I, _VP]),
     "ffa_last_error": (_I, [ctypes.c_char_p, _I]),
     "ffa_device_status": (_I, [ctypes.POINTER(ctypes.c_uint)]),

@@ -144,6 +144,31 @@ __device__ __forceinline__ void stage_acc_half(uint32_t t_acc, int g, uint32_t t
   }
 }
 
+// Add the accumulator columns [g*D/2, (g+1)*D/2) of this lane, times `mul`, to the fp32
+// row `dst` (D floats, 16-byte aligned) when `valid`.  Every lane of the warp must call
+// it (tcgen05.ld is warp-wide); lanes past the end pass valid = false.
+template <int D>
+__device__ __forceinline__ void add_acc_half(uint32_t t_acc, int g, float* dst, bool valid, float mul) {
+#pragma unroll 1
+  for (int c = g * (D / 64); c < (g + 1) * (D / 64); ++c) {
+    uint32_t r[32];
+    tmem_ld32(t_acc + 32 * c, r);
+    tmem_ld_wait();
+    if (valid) {
+      float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float4 a = d4[e];
+        a.x = fmaf(__uint_as_float(r[4 * e + 0]), mul, a.x);
+        a.y = fmaf(__uint_as_float(r[4 * e + 1]), mul, a.y);
+        a.z = fmaf(__uint_as_float(r[4 * e + 2]), mul, a.z);
+        a.w = fmaf(__uint_as_float(r[4 * e + 3]), mul, a.w);
+        d4[e] = a;
+      }
+    }
+  }
+}
+
 // Every one of the 256 compute threads calls this, staged or not (a thread that left its
 // loop early after a timeout passes staged = false): it is a barrier for all of them.  If
 // all staged their rows, one thread stores the tiles (64-column boxes) with TMA and waits
@@ -168,13 +193,15 @@ __device__ __forceinline__ void store_staged(bool staged, const CUtensorMap* con
 // ====================================================================================
 // dK / dV
 // ====================================================================================
-template <int D, bool CAUSAL>
+// ACC: accumulate mode (ffa_bwd_dkdv_acc), a separate instantiation so the plain kernel
+// keeps its register allocation.
+template <int D, bool CAUSAL, bool ACC>
 __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     ffa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                         const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                         const float* __restrict__ LSE, const float* __restrict__ DELTA,
-                        __nv_bfloat16* __restrict__ DK, __nv_bfloat16* __restrict__ DV, int S, int BH, int group,
+                        float* __restrict__ DK_ACC, float* __restrict__ DV_ACC, int S, int BH, int group,
                         long long stride_bh, long long stride_s, float scale_log2, float scale) {
   using L = bwd::DkdvLayout<D>;
   constexpr int SLABS = D / 64;
@@ -501,14 +528,22 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       mbar_arrive(ds_ready);
     }
     const bool staged = ok && nq > 0 && mbar_wait(final_bar, 0, abort_flag, kErrBwdCompute);
+    constexpr bool acc_mode = ACC;
     if (staged) {
-      // every MMA has finished: the Q ring is free and holds the staged dV, dK tiles
       tc_fence_after();
-      bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::Q_OFF, row, 1.f);
-      bwd::stage_acc_half<D>(tmem + lane_off + 384, g, sbase + L::Q_OFF + L::TILE, row, scale);
+      if constexpr (acc_mode) {
+        // fp32 accumulate: this CTA is the only writer of its key rows in this launch
+        const long long off = (static_cast<long long>(bh) * S + kg) * D;
+        bwd::add_acc_half<D>(tmem + lane_off + 256, g, DV_ACC + off, kg < S, 1.f);
+        bwd::add_acc_half<D>(tmem + lane_off + 384, g, DK_ACC + off, kg < S, scale);
+      } else {
+        // every MMA has finished: the Q ring is free and holds the staged dV, dK tiles
+        bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::Q_OFF, row, 1.f);
+        bwd::stage_acc_half<D>(tmem + lane_off + 384, g, sbase + L::Q_OFF + L::TILE, row, scale);
+      }
     }
     const CUtensorMap* const maps[2] = {&tm_dv, &tm_dk};
-    bwd::store_staged<D, 2>(staged, maps, sbase + L::Q_OFF, n0, bh);
+    bwd::store_staged<D, 2>(staged && !acc_mode, maps, sbase + L::Q_OFF, n0, bh);
   }
 
   tc_fence_before();
@@ -525,12 +560,13 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 // TMEM: S double buffer at columns 0 and 384, dP at 128, dQ at 256.
 __device__ __forceinline__ uint32_t dq_sbuf(int b) { return b ? 384u : 0u; }
 
-template <int D, bool CAUSAL>
+// ACC: accumulate mode (ffa_bwd_dq_acc).
+template <int D, bool CAUSAL, bool ACC>
 __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_dq,
-                      const float* __restrict__ LSE, const float* __restrict__ DELTA, __nv_bfloat16* __restrict__ DQ,
+                      const float* __restrict__ LSE, const float* __restrict__ DELTA, float* __restrict__ DQ_ACC,
                       int S, int BH, int group, long long stride_bh, long long stride_s, float scale_log2,
                       float scale) {
   using L = bwd::DqLayout<D>;
@@ -779,13 +815,16 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(11 + 4 * g, j);
     }
     const bool staged = ok && nk > 0 && mbar_wait(final_bar, 0, abort_flag, kErrDqCompute);
+    constexpr bool acc_mode = ACC;
     if (staged) {
-      // every MMA has finished: the K ring is free and holds the staged dQ tile
       tc_fence_after();
-      bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::K_OFF, row, scale);
+      if constexpr (acc_mode)  // fp32 accumulate: this CTA is the only writer of its query rows
+        bwd::add_acc_half<D>(tmem + lane_off + 256, g, DQ_ACC + ridx * D, qg < S, scale);
+      else  // every MMA has finished: the K ring is free and holds the staged dQ tile
+        bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::K_OFF, row, scale);
     }
     const CUtensorMap* const maps[1] = {&tm_dq};
-    bwd::store_staged<D, 1>(staged, maps, sbase + L::K_OFF, m0, bh);
+    bwd::store_staged<D, 1>(staged && !acc_mode, maps, sbase + L::K_OFF, m0, bh);
   }
 
   tc_fence_before();
@@ -799,7 +838,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 // host launchers
 // ------------------------------------------------------------------------------------
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool ACC>
 static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   using LK = bwd::DkdvLayout<D>;
   CUtensorMap tk, tv, tq, tdo;
@@ -809,16 +848,16 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   CUtensorMap tdk, tdv;
-  if ((rc = make_tile_map(&tdk, a.dk, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tdv, a.dv, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  auto kern = ffa_bwd_dkdv_kernel<D, CAUSAL>;
+  // accumulate mode stores nothing through these maps: any valid tensor serves as their base
+  if ((rc = make_tile_map(&tdk, a.dk_acc ? a.k : a.dk, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  if ((rc = make_tile_map(&tdv, a.dv_acc ? a.v : a.dv, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  auto kern = ffa_bwd_dkdv_kernel<D, CAUSAL, ACC>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LK::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid(static_cast<unsigned>((a.S + bwd::LANES - 1) / bwd::LANES) * static_cast<unsigned>(a.BH));
-  kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, tdk, tdv, a.lse, a.delta,
-                                                        static_cast<__nv_bfloat16*>(a.dk),
-                                                        static_cast<__nv_bfloat16*>(a.dv), a.S, a.BH,
+  kern<<<grid, bwd::NTHREADS, LK::SMEM_BYTES, stream>>>(tk, tv, tq, tdo, tdk, tdv, a.lse, a.delta, a.dk_acc,
+                                                        a.dv_acc, a.S, a.BH,
                                                         work_group(a.BH, a.S, D, CAUSAL), a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
                                                         static_cast<float>(a.scale));
@@ -827,7 +866,7 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
   return FFA_OK;
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool ACC>
 static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   using LQ = bwd::DqLayout<D>;
   CUtensorMap tq, tdo, tk, tv;
@@ -837,14 +876,13 @@ static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   CUtensorMap tdq;
-  if ((rc = make_tile_map(&tdq, a.dq, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  auto kern = ffa_bwd_dq_kernel<D, CAUSAL>;
+  if ((rc = make_tile_map(&tdq, a.dq_acc ? a.q : a.dq, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
+  auto kern = ffa_bwd_dq_kernel<D, CAUSAL, ACC>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid(static_cast<unsigned>((a.S + bwd::LANES - 1) / bwd::LANES) * static_cast<unsigned>(a.BH));
-  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, tdq, a.lse, a.delta,
-                                                        static_cast<__nv_bfloat16*>(a.dq), a.S, a.BH,
+  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, tdq, a.lse, a.delta, a.dq_acc, a.S, a.BH,
                                                         work_group(a.BH, a.S, D, CAUSAL), a.stride_bh,
                                                         a.stride_s, static_cast<float>(a.scale * kLog2e),
                                                         static_cast<float>(a.scale));
@@ -853,64 +891,95 @@ static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   return FFA_OK;
 }
 
+template <int D, bool CAUSAL>
+static int launch_dkdv_a(const BwdArgs& a, cudaStream_t stream) {
+  return a.dk_acc ? launch_dkdv_t<D, CAUSAL, true>(a, stream) : launch_dkdv_t<D, CAUSAL, false>(a, stream);
+}
+
+template <int D, bool CAUSAL>
+static int launch_dq_a(const BwdArgs& a, cudaStream_t stream) {
+  return a.dq_acc ? launch_dq_t<D, CAUSAL, true>(a, stream) : launch_dq_t<D, CAUSAL, false>(a, stream);
+}
+
 int launch_dkdv(const BwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_dkdv_t<128, true>(a, stream) : launch_dkdv_t<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_dkdv_t<64, true>(a, stream) : launch_dkdv_t<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_dkdv_a<128, true>(a, stream) : launch_dkdv_a<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_dkdv_a<64, true>(a, stream) : launch_dkdv_a<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 
 int launch_dq(const BwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_dq_t<128, true>(a, stream) : launch_dq_t<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_dq_t<64, true>(a, stream) : launch_dq_t<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_dq_a<128, true>(a, stream) : launch_dq_a<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_dq_a<64, true>(a, stream) : launch_dq_a<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 
-// A second stream per device (created on first use, never destroyed) on which dQ runs
-// beside dK/dV: the two kernels are independent once delta exists, and CTAs of one fill
-// the SMs the other leaves idle at its tail.  Fork and join are event waits, so the
-// pair also records correctly into a CUDA graph captured on the caller's stream.
-// The caller holds bwd_fork_mutex() (the events are shared by every caller on a device).
+// A second stream on which dQ runs beside dK/dV: the two kernels are independent once
+// delta exists, and CTAs of one fill the SMs the other leaves idle at its tail.  Fork and
+// join are event waits, so the pair also records correctly into a CUDA graph captured on
+// the caller's stream.
+//
+// Each (device, caller stream) pair gets its own side stream and events, created on its
+// first backward and kept until exit.  A capture on one caller stream pulls that caller's
+// side stream into the capture until the capture ends; keeping side streams apart per
+// caller stream means a plain backward issued meanwhile on another stream (another thread)
+// never lands in that graph.  Past kMaxSideStreams pairs, dQ runs on the caller's stream
+// after dK/dV instead (same results, no overlap).  The caller holds bwd_fork_mutex().
 static std::mutex& bwd_fork_mutex() {
   static std::mutex mu;
   return mu;
 }
 
-static int side_stream(cudaStream_t* out, cudaEvent_t* fork, cudaEvent_t* join) {
-  struct Side { cudaStream_t s; cudaEvent_t f, j; };
-  static Side side[64] = {};
-  static int ready[64] = {0};
+struct SideStream {
+  int dev;
+  cudaStream_t caller;
+  cudaStream_t s;
+  cudaEvent_t f, j;
+};
+constexpr int kMaxSideStreams = 256;
+
+// Side stream and events of (current device, caller); *out = nullptr when the table is
+// full.  Returns FFA_OK or an error when creating them failed.
+static int side_stream(cudaStream_t caller, SideStream** out) {
+  static SideStream table[kMaxSideStreams];
+  static int used = 0;
+  *out = nullptr;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_error(FFA_ERR_LAUNCH, "cudaGetDevice failed");
-  Side& sd = side[dev & 63];
-  {
-    if (!ready[dev & 63]) {
-      if (cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking) != cudaSuccess ||
-          cudaEventCreateWithFlags(&sd.f, cudaEventDisableTiming) != cudaSuccess ||
-          cudaEventCreateWithFlags(&sd.j, cudaEventDisableTiming) != cudaSuccess)
-        return set_error(FFA_ERR_LAUNCH, "could not create the backward's side stream");
-      ready[dev & 63] = 1;
+  for (int i = 0; i < used; ++i)
+    if (table[i].dev == dev && table[i].caller == caller) {
+      *out = &table[i];
+      return FFA_OK;
     }
-  }
-  *out = sd.s;
-  *fork = sd.f;
-  *join = sd.j;
+  if (used == kMaxSideStreams) return FFA_OK;
+  SideStream& sd = table[used];
+  sd.dev = dev;
+  sd.caller = caller;
+  if (cudaStreamCreateWithFlags(&sd.s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&sd.f, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&sd.j, cudaEventDisableTiming) != cudaSuccess)
+    return set_error(FFA_ERR_LAUNCH, "could not create the backward's side stream");
+  ++used;
+  *out = &sd;
   return FFA_OK;
 }
 
 int launch_bwd(const BwdArgs& a, cudaStream_t stream) {
   int rc;
   if ((rc = launch_preprocess(a.o, a.dout, a.delta, a.BH, a.S, a.D, a.stride_bh, a.stride_s, stream))) return rc;
-  // record / wait / launch as one unit: another thread's backward on this device must not
-  // re-record the shared events in between
+  // record / wait / launch as one unit: another thread's backward on the same caller
+  // stream must not re-record the shared events in between
   std::lock_guard<std::mutex> lock(bwd_fork_mutex());
-  cudaStream_t side;
-  cudaEvent_t fork, join;
-  if ((rc = side_stream(&side, &fork, &join))) return rc;
-  if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
+  SideStream* sd = nullptr;
+  if ((rc = side_stream(stream, &sd))) return rc;
+  if (sd == nullptr) {  // side-stream table full: serial on the caller's stream
+    if ((rc = launch_dkdv(a, stream))) return rc;
+    return launch_dq(a, stream);
+  }
+  if (cudaEventRecord(sd->f, stream) != cudaSuccess || cudaStreamWaitEvent(sd->s, sd->f, 0) != cudaSuccess)
     return set_error(FFA_ERR_LAUNCH, "backward fork failed");
-  if ((rc = launch_dq(a, side))) return rc;
+  if ((rc = launch_dq(a, sd->s))) return rc;
   if ((rc = launch_dkdv(a, stream))) return rc;
-  if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
+  if (cudaEventRecord(sd->j, sd->s) != cudaSuccess || cudaStreamWaitEvent(stream, sd->j, 0) != cudaSuccess)
     return set_error(FFA_ERR_LAUNCH, "backward join failed");
   return FFA_OK;
 }

@@ -178,7 +178,7 @@ static int check_common(int BH, int S, int D, long long stride_bh, long long str
   if (BH > 1 && (stride_bh < static_cast<long long>(S) * stride_s || stride_bh % 8 != 0))
     return set_error(FFA_ERR_INVALID, "stride_bh must be >= S*stride_s and a multiple of 8");
   // the kernels run one CTA per 128-row block of every slice in a 1-D grid
-  if (static_cast<long long>((S + 127) / 128) * BH > 2147483647LL)
+  if ((static_cast<long long>(S) + 127) / 128 * BH > 2147483647LL)
     return set_error(FFA_ERR_UNSUPPORTED, "BH * ceil(S/128) exceeds the grid limit of 2^31-1 CTAs");
   return FFA_OK;
 }
@@ -199,6 +199,19 @@ int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, in
     return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
   if ((rc = ensure_context()) != FFA_OK) return rc;
   FwdArgs a{q, k, v, o, lse, BH, S, D, stride_bh, stride_s, scale, causal};
+  return launch_fwd(a, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_fwd_merge(const void* q, const void* k, const void* v, float* acc, float* acc_lse, int BH, int S, int D,
+                  long long stride_bh, long long stride_s, double scale, int causal, int first, void* stream) {
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !acc || !acc_lse) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(acc))
+    return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
+  FwdArgs a{q, k, v, nullptr, nullptr, BH, S, D, stride_bh, stride_s, scale, causal, acc, acc_lse, first ? 1 : 0};
   return launch_fwd(a, static_cast<cudaStream_t>(stream));
 }
 
@@ -282,6 +295,40 @@ int ffa_bwd_dq(const void* q, const void* k, const void* v, const void* dout, co
                void* stream) {
   return bwd_part(q, k, v, dout, lse, delta, dq, nullptr, nullptr, BH, S, D, stride_bh, stride_s, scale, causal,
                   stream, false);
+}
+
+int ffa_bwd_dkdv_acc(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                     const float* delta, float* dk_acc, float* dv_acc, int BH, int S, int D, long long stride_bh,
+                     long long stride_s, double scale, int causal, void* stream) {
+  if (!dk_acc || !dv_acc) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(dk_acc) || !aligned16(dv_acc)) return set_error(FFA_ERR_INVALID, "accumulators must be 16-byte aligned");
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !dout || !lse || !delta) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  for (const void* p : {q, k, v, dout})
+    if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
+  BwdArgs a{q, k, v, nullptr, dout, lse, const_cast<float*>(delta), nullptr, nullptr, nullptr, BH, S, D, stride_bh,
+            stride_s, scale, causal, nullptr, dk_acc, dv_acc};
+  return launch_dkdv(a, static_cast<cudaStream_t>(stream));
+}
+
+int ffa_bwd_dq_acc(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+                   float* dq_acc, int BH, int S, int D, long long stride_bh, long long stride_s, double scale,
+                   int causal, void* stream) {
+  if (!dq_acc) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(dq_acc)) return set_error(FFA_ERR_INVALID, "accumulators must be 16-byte aligned");
+  int rc = check_common(BH, S, D, stride_bh, stride_s);
+  if (rc) return rc;
+  if (BH == 0 || S == 0) return FFA_OK;
+  if (!q || !k || !v || !dout || !lse || !delta) return set_error(FFA_ERR_INVALID, "null tensor pointer");
+  for (const void* p : {q, k, v, dout})
+    if (!aligned16(p)) return set_error(FFA_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if ((rc = ensure_context()) != FFA_OK) return rc;
+  BwdArgs a{q, k, v, nullptr, dout, lse, const_cast<float*>(delta), nullptr, nullptr, nullptr, BH, S, D, stride_bh,
+            stride_s, scale, causal, dq_acc, nullptr, nullptr};
+  return launch_dq(a, static_cast<cudaStream_t>(stream));
 }
 
 int ffa_lse_merge(float* acc, float* acc_lse, const void* part, const float* part_lse, long long rows, int D,

@@ -39,6 +39,11 @@ struct FwdArgs {
   long long stride_bh, stride_s;
   double scale;
   int causal;
+  // merge mode (ffa_fwd_merge): fold this call's result into a running fp32 result
+  // acc [BH, S, D] (row stride D) with base-2 LSE acc_lse [BH, S]; `first` initialises it
+  float* acc = nullptr;
+  float* acc_lse = nullptr;
+  int first = 0;
 };
 
 struct BwdArgs {
@@ -56,6 +61,11 @@ struct BwdArgs {
   long long stride_bh, stride_s;
   double scale;
   int causal;
+  // accumulate mode (ffa_bwd_dkdv_acc / ffa_bwd_dq_acc): add the gradients in fp32 into
+  // [BH, S, D] buffers (row stride D) instead of writing bf16 dq / dk / dv
+  float* dq_acc = nullptr;
+  float* dk_acc = nullptr;
+  float* dv_acc = nullptr;
 };
 
 // Work of a CTA in a 1-D grid of nblk x BH CTAs: its block rank (rank 0 = the block

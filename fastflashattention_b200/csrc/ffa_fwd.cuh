@@ -26,8 +26,6 @@
 // rescaled only when a row's max grows by more than 2^8, which keeps every P <= 256
 // (exact in fp32 / bf16 range).  CTAs run in longest-job-first order (cta_work).
 #pragma once
-#include <cstdlib>
-
 #include "ffa_common.cuh"
 
 namespace ffa {
@@ -95,12 +93,15 @@ __device__ __forceinline__ float row_max128(const float (&s)[fwd::BN]) {
   return fmax3(fmax3(b0, b1, b2), fmax3(b3, b4, a[15]), b0);
 }
 
-template <int D, bool CAUSAL, int EMU = fwd::emu_pairs<D>(), bool SEQ = fwd::seq_turns<D>()>
+// MERGE: the ring's merge mode (ffa_fwd_merge); its epilogue folds the result into an
+// fp32 running result instead of storing bf16 O (a separate instantiation, so the plain
+// forward keeps its register allocation).
+template <int D, bool CAUSAL, bool MERGE, int EMU = fwd::emu_pairs<D>(), bool SEQ = fwd::seq_turns<D>()>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                    float* __restrict__ LSE, int S, int BH, int group,
-                   float scale_log2) {
+                   float scale_log2, float* __restrict__ ACC, float* __restrict__ ACC_LSE, int first) {
   using L = fwd::Layout<D>;
   constexpr int SLABS = D / 64;
   extern __shared__ uint8_t smem_raw[];
@@ -436,7 +437,43 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     // warpgroup reaches the barrier, finished or not, so none can wait for one that left.
     const bool staged = ok && nt > 0 && mbar_wait(o_final(i), 0, abort_flag, kErrFwdSoftmax);
     const uint32_t o_tile = sbase + L::Q_OFF + i * L::TILE_BYTES;
-    if (staged) {
+    if constexpr (MERGE) {
+      // Merge mode: fold this result (O = acc/l, base-2 LSE lp) into the running fp32
+      // result of its rows: w_a = 2^(la - m), w_b = 2^(lp - m), m = max(la, lp);
+      // acc = (w_a acc + w_b O) / (w_a + w_b), acc_lse = m + log2(w_a + w_b).  This
+      // thread's row has no other writer in the launch.
+      if (staged) {
+        tc_fence_after();
+        const bool valid = grow < S;
+        const long long idx = static_cast<long long>(bh) * S + grow;
+        const float lp = (l == 0.f) ? -INFINITY : m_used + log2f(l);
+        const float la = (first || !valid) ? -INFINITY : ACC_LSE[idx];
+        const float mm = fmaxf(la, lp);
+        const float wa = (mm == -INFINITY) ? 1.f : exp2f(la - mm);
+        const float wb = (mm == -INFINITY) ? 0.f : exp2f(lp - mm);
+        const float inv = 1.f / (wa + wb);
+        const float ca = wa * inv, cb = (l == 0.f) ? 0.f : wb * inv / l;
+        float* dst = ACC + idx * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_o + c * 32, r);
+          tmem_ld_wait();
+          if (valid) {
+            float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float4 a = first ? make_float4(0.f, 0.f, 0.f, 0.f) : d4[e];
+              d4[e] = make_float4(fmaf(a.x, ca, __uint_as_float(r[4 * e + 0]) * cb),
+                                  fmaf(a.y, ca, __uint_as_float(r[4 * e + 1]) * cb),
+                                  fmaf(a.z, ca, __uint_as_float(r[4 * e + 2]) * cb),
+                                  fmaf(a.w, ca, __uint_as_float(r[4 * e + 3]) * cb));
+            }
+          }
+        }
+        if (valid) ACC_LSE[idx] = (mm == -INFINITY) ? -INFINITY : mm + log2f(wa + wb);
+      }
+    } else if (staged) {
       tc_fence_after();
       const float l_safe = (l == 0.f) ? 1.f : l;
       const float inv_l = 1.f / l_safe;
@@ -453,7 +490,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
       }
     }
     fence_proxy_async_smem();
-    if (named_barrier_and(1 + i, 128, staged) && row == 0) {
+    if (named_barrier_and(1 + i, 128, staged && !MERGE) && row == 0) {
 #pragma unroll
       for (int sl = 0; sl < SLABS; ++sl) tma_store_3d(&tm_o, o_tile + sl * 16384, sl * 64, mi, bh);
       bulk_commit_group();
@@ -472,7 +509,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 // host launcher
 // ------------------------------------------------------------------------------------
-template <int D, bool CAUSAL, int EMU, bool SEQ>
+template <int D, bool CAUSAL, bool MERGE>
 static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   using L = fwd::Layout<D>;
   CUtensorMap tq, tk, tv;
@@ -480,9 +517,9 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  CUtensorMap to;
-  if ((rc = make_tile_map(&to, a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  auto kern = ffa_fwd_kernel<D, CAUSAL, EMU, SEQ>;
+  CUtensorMap to;  // merge mode stores nothing through it: q serves as its base
+  if ((rc = make_tile_map(&to, a.acc ? a.q : a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
+  auto kern = ffa_fwd_kernel<D, CAUSAL, MERGE>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   // The setmaxnreg split assumes the kernel is launched with 168 registers per thread;
@@ -499,52 +536,21 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   const int n_mblk = (a.S + 2 * fwd::BM - 1) / (2 * fwd::BM);
   const dim3 grid(static_cast<unsigned>(n_mblk) * static_cast<unsigned>(a.BH));
   kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, to, a.lse, a.S, a.BH, work_group(a.BH, a.S, D, CAUSAL),
-                                                        static_cast<float>(a.scale * kLog2e));
+                                                        static_cast<float>(a.scale * kLog2e), a.acc, a.acc_lse,
+                                                        a.first);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
   return FFA_OK;
 }
 
-// Share of exponentials taken on the FMA pipe, in column pairs out of 8: fwd::emu_pairs<D>()
-// unless FFA_FWD_EMU=0..2 overrides it (for measurements only).
-static int fwd_emu_override() {
-  static const int v = [] {
-    const char* e = std::getenv("FFA_FWD_EMU");
-    if (e == nullptr || e[0] < '0' || e[0] > '2' || e[1] != '\0') return -1;
-    return e[0] - '0';
-  }();
-  return v;
-}
-
-// fwd::seq_turns<D>() unless FFA_FWD_SEQ=0/1 overrides it (for measurements only).
-template <int D>
-static bool fwd_seq() {
-  static const bool v = [] {
-    const char* e = std::getenv("FFA_FWD_SEQ");
-    if (e != nullptr && (e[0] == '0' || e[0] == '1') && e[1] == '\0') return e[0] == '1';
-    return fwd::seq_turns<D>();
-  }();
-  return v;
-}
-
-template <int D, bool CAUSAL, bool SEQ>
-static int launch_fwd_emu(const FwdArgs& a, cudaStream_t stream) {
-  const int o = fwd_emu_override();
-  switch (o < 0 ? fwd::emu_pairs<D>() : o) {
-    case 0: return launch_fwd_t<D, CAUSAL, 0, SEQ>(a, stream);
-    case 1: return launch_fwd_t<D, CAUSAL, 1, SEQ>(a, stream);
-    default: return launch_fwd_t<D, CAUSAL, 2, SEQ>(a, stream);
-  }
-}
-
 template <int D, bool CAUSAL>
-static int launch_fwd_seq(const FwdArgs& a, cudaStream_t stream) {
-  return fwd_seq<D>() ? launch_fwd_emu<D, CAUSAL, true>(a, stream) : launch_fwd_emu<D, CAUSAL, false>(a, stream);
+static int launch_fwd_m(const FwdArgs& a, cudaStream_t stream) {
+  return a.acc ? launch_fwd_t<D, CAUSAL, true>(a, stream) : launch_fwd_t<D, CAUSAL, false>(a, stream);
 }
 
 int launch_fwd(const FwdArgs& a, cudaStream_t stream) {
-  if (a.D == 128) return a.causal ? launch_fwd_seq<128, true>(a, stream) : launch_fwd_seq<128, false>(a, stream);
-  if (a.D == 64) return a.causal ? launch_fwd_seq<64, true>(a, stream) : launch_fwd_seq<64, false>(a, stream);
+  if (a.D == 128) return a.causal ? launch_fwd_m<128, true>(a, stream) : launch_fwd_m<128, false>(a, stream);
+  if (a.D == 64) return a.causal ? launch_fwd_m<64, true>(a, stream) : launch_fwd_m<64, false>(a, stream);
   return set_error(FFA_ERR_UNSUPPORTED, "kernel head_dim must be 64 or 128");
 }
 

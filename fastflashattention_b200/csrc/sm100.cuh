@@ -415,7 +415,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // the nearest integer (obtained by adding and subtracting the shifter 1.5*2^23) and
 // f in [-1/2, 1/2]; 2^f from a degree-3 polynomial whose coefficients minimise the
 // maximum relative error on that interval (Remez exchange, derived by
-// csrc/fit_exp2_poly.py; max relative error 7.5e-5, 25x below bf16's half-ulp);
+// tests/test_exp2_poly.py, which re-derives them; max relative error 7.5e-5, 25x below
+// bf16's half-ulp; x <= -126 returns about 2^-126, not 0);
 // 2^n is applied by adding n to the exponent field.  Offloading part of the softmax
 // exponentials here keeps MUFU.EX2 (16/clk/SM) from capping the tensor core.
 __device__ __forceinline__ float exp2_fma(float x) {

@@ -35,6 +35,19 @@ extern "C" {
 int ffa_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int BH, int S, int D,
             long long stride_bh, long long stride_s, double scale, int causal, void* stream);
 
+/* Forward of one block of a context-parallel ring, merged into a running result (no
+ * reference counterpart: the reference has no sequence parallelism; this builds on the
+ * base-2 LSE that `_fastflash_fwd` writes, _kernel.py:274-279).  Computes the attention of
+ * q over this call's k, v exactly as ffa_fwd does, then folds it, in fp32 and without
+ * rounding it to bf16, into
+ *   acc     : [BH, S, D] fp32, rows D floats apart, slices S*D apart (16-byte aligned)
+ *   acc_lse : [BH, S] fp32 base-2 LSE of acc
+ * as acc = (2^acc_lse acc + 2^lse O) / (2^acc_lse + 2^lse), acc_lse = log2 of the
+ * denominator.  `first` != 0 initialises acc and acc_lse instead (their contents are not
+ * read).  Each row has one writer, so the result does not depend on scheduling. */
+int ffa_fwd_merge(const void* q, const void* k, const void* v, float* acc, float* acc_lse, int BH, int S, int D,
+                  long long stride_bh, long long stride_s, double scale, int causal, int first, void* stream);
+
 /* Backward preprocess: delta[bh, i] = sum_d O[bh,i,d] * dO[bh,i,d] in fp32.
  * Replaces `_bwd_preprocess` / `_uni_bwd_preprocess` (_kernel.py:323-351). */
 int ffa_bwd_preprocess(const void* o, const void* dout, float* delta, int BH, int S, int D,
@@ -44,6 +57,9 @@ int ffa_bwd_preprocess(const void* o, const void* dout, float* delta, int BH, in
  * (query-block grid), each output tile written by exactly one CTA, no atomics.
  * Replaces `FastFlashAttn.backward` (_kernel.py:784-906) with its kernels
  * `_uni_bwd_dkdv` (:379-448) and `_uni_bwd_dq` (:487-564).
+ * dQ runs on a side stream beside dK/dV; each (device, caller stream) pair gets its own
+ * side stream and events on its first call (kept until exit), joined back with events,
+ * so the call records correctly into a CUDA graph captured on `stream`.
  *   lse      : [BH, S] fp32 from ffa_fwd
  *   delta_ws : [BH, S] fp32 caller-provided workspace (receives delta)
  *   dq,dk,dv : [BH, S, D] bf16 outputs (same strides as q) */
@@ -60,7 +76,9 @@ int ffa_bwd(const void* q, const void* k, const void* v, const void* o, const vo
  * fixed 16 MiB array inside the library (held on every GPU that loads the library
  * until the process exits), so BH*S must be <= 4194304 (else FFA_ERR_INVALID).
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * (cudaGetSymbolAddress), and the first call on each (device, stream) pair creates
+ * the backward's side stream and its two events (as ffa_bwd does); make those first
+ * calls outside any stream capture.
  * All calls share the one array: calls that overlap on the GPU race — serialise them. */
 int ffa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
                     void* dq, void* dk, void* dv, int BH, int S, int D, long long stride_bh, long long stride_s,
@@ -77,6 +95,20 @@ int ffa_bwd_dkdv(const void* q, const void* k, const void* v, const void* dout, 
 int ffa_bwd_dq(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
                void* dq, int BH, int S, int D, long long stride_bh, long long stride_s, double scale, int causal,
                void* stream);
+
+/* ffa_bwd_dkdv / ffa_bwd_dq that ADD their gradients, in fp32 and unrounded, into caller
+ * accumulators instead of writing bf16 (the ring backward sums the blocks of one key or
+ * query chunk there; the reference has no counterpart, see ffa_fwd_merge):
+ *   dk_acc += scale * dS^T Q,  dv_acc += P^T dO,  dq_acc += scale * dS K
+ * Accumulators are [BH, S, D] fp32, rows D floats apart, slices S*D apart, 16-byte
+ * aligned.  Every accumulator row has exactly one writer per call, so repeated calls in a
+ * fixed order give bitwise-reproducible sums. */
+int ffa_bwd_dkdv_acc(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+                     const float* delta, float* dk_acc, float* dv_acc, int BH, int S, int D, long long stride_bh,
+                     long long stride_s, double scale, int causal, void* stream);
+int ffa_bwd_dq_acc(const void* q, const void* k, const void* v, const void* dout, const float* lse, const float* delta,
+                   float* dq_acc, int BH, int S, int D, long long stride_bh, long long stride_s, double scale,
+                   int causal, void* stream);
 
 /* Merge of partial attention results for the context-parallel ring (no reference
  * counterpart: the reference has no sequence parallelism; it builds on the base-2 LSE

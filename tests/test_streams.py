@@ -69,3 +69,52 @@ def test_backward_in_cuda_graph_replays_eager_result():
     torch.cuda.synchronize()
     for a, b in zip(want, out):
         assert torch.equal(a, b)
+
+
+def test_capture_beside_plain_backward_on_another_thread():
+    """One thread captures a backward into a CUDA graph while another runs plain backward
+    passes on its own stream.  Side streams are kept per caller stream, so the plain
+    passes never land in the graph: both the plain results and the graph's replay equal
+    the sequential results."""
+    cap_in = _inputs(21, B=2, H=2, S=900)
+    plain_in = _inputs(22)
+    want_cap = _bwd(*cap_in, True, None)
+    want_plain = _bwd(*plain_in, True, None)
+    torch.cuda.synchronize()
+    cs, ps = torch.cuda.Stream(), torch.cuda.Stream()
+    with torch.cuda.stream(cs):  # first backward on this caller stream outside capture
+        _bwd(*cap_in, True, None)
+    cs.synchronize()
+    started, errors, plain_out = threading.Event(), [], []
+
+    def plain():
+        try:
+            started.wait(timeout=60)
+            with torch.cuda.stream(ps):
+                for _ in range(5):
+                    plain_out.append(_bwd(*plain_in, True, None))
+            ps.synchronize()
+        except Exception as e:  # noqa: BLE001 - reported below
+            errors.append(e)
+
+    t = threading.Thread(target=plain)
+    t.start()
+    g = torch.cuda.CUDAGraph()
+    # "thread_local" keeps the other thread's plain launches legal during this capture
+    with torch.cuda.graph(g, stream=cs, capture_error_mode="thread_local"):
+        started.set()
+        out = _bwd(*cap_in, True, None)
+        for _ in range(20):  # stay in capture while the other thread launches
+            out = _bwd(*cap_in, True, None)
+    t.join(timeout=120)
+    assert not errors, errors
+    for x in out:
+        x.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(want_cap, out):
+        assert torch.equal(a, b)
+    assert plain_out
+    for res in plain_out:
+        for a, b in zip(want_plain, res):
+            assert torch.equal(a, b)
