@@ -73,44 +73,49 @@ def block_kind(x: int, y: int) -> str | None:
 
 # ------------------------------------------------------------------------ block ops
 class CudaBlockOps:
-    """Per-block kernels on the sm_100a library (tensors [BH, C, D] contiguous bf16)."""
+    """Per-block kernels on the sm_100a library (tensors [BH, C, D] contiguous; bf16 inputs,
+    fp32 accumulators).  Partial results never round to bf16: the forward folds each block
+    into an fp32 running result in its epilogue (``ffa_fwd_merge``) and the backward adds
+    each block's gradients into fp32 accumulators (``ffa_bwd_dkdv_acc`` / ``ffa_bwd_dq_acc``),
+    dQ on a side stream beside dK/dV."""
 
-    def fwd(self, q, k, v, causal: bool, scale: float):
+    def __init__(self):
+        self._side = {}
+
+    def _stream(self, t):
+        return torch.cuda.current_stream(t.device).cuda_stream
+
+    def fwd_merge(self, q, k, v, causal: bool, scale: float, acc, acc_lse, first: bool):
         BH, C, D = q.shape
-        o = torch.empty_like(q)
-        lse = torch.empty(BH, C, device=q.device, dtype=torch.float32)
         lib = _lib.load()
-        _lib.check(lib.ffa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), BH, C, D,
-                               C * D, D, scale, int(causal), torch.cuda.current_stream(q.device).cuda_stream),
-                   "ffa_fwd")
-        return o, lse
-
-    def merge(self, acc, acc_lse, o, lse, first: bool):
-        BH, C, D = o.shape
-        lib = _lib.load()
-        _lib.check(lib.ffa_lse_merge(acc.data_ptr(), acc_lse.data_ptr(), o.data_ptr(), lse.data_ptr(), BH * C, D,
-                                     int(first), torch.cuda.current_stream(o.device).cuda_stream), "ffa_lse_merge")
+        _lib.check(lib.ffa_fwd_merge(q.data_ptr(), k.data_ptr(), v.data_ptr(), acc.data_ptr(), acc_lse.data_ptr(),
+                                     BH, C, D, C * D, D, scale, int(causal), int(first), self._stream(q)),
+                   "ffa_fwd_merge")
 
     def delta(self, o, do):
         BH, C, D = o.shape
         d = torch.empty(BH, C, device=o.device, dtype=torch.float32)
         lib = _lib.load()
         _lib.check(lib.ffa_bwd_preprocess(o.data_ptr(), do.data_ptr(), d.data_ptr(), BH, C, D, C * D, D,
-                                          torch.cuda.current_stream(o.device).cuda_stream), "ffa_bwd_preprocess")
+                                          self._stream(o)), "ffa_bwd_preprocess")
         return d
 
-    def bwd(self, q, k, v, do, lse, delta, causal: bool, scale: float):
+    def bwd_acc(self, q, k, v, do, lse, delta, causal: bool, scale: float, dq_acc, dk_acc, dv_acc):
         BH, C, D = q.shape
-        dq, dk, dv = (torch.empty_like(q) for _ in range(3))
         lib = _lib.load()
-        st = torch.cuda.current_stream(q.device).cuda_stream
-        _lib.check(lib.ffa_bwd_dkdv(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
-                                    delta.data_ptr(), dk.data_ptr(), dv.data_ptr(), BH, C, D, C * D, D, scale,
-                                    int(causal), st), "ffa_bwd_dkdv")
-        _lib.check(lib.ffa_bwd_dq(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
-                                  delta.data_ptr(), dq.data_ptr(), BH, C, D, C * D, D, scale, int(causal), st),
-                   "ffa_bwd_dq")
-        return dq, dk, dv
+        cur = torch.cuda.current_stream(q.device)
+        side = self._side.get(q.device)
+        if side is None:
+            side = self._side[q.device] = torch.cuda.Stream(device=q.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            _lib.check(lib.ffa_bwd_dq_acc(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                          delta.data_ptr(), dq_acc.data_ptr(), BH, C, D, C * D, D, scale,
+                                          int(causal), side.cuda_stream), "ffa_bwd_dq_acc")
+        _lib.check(lib.ffa_bwd_dkdv_acc(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                        delta.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(), BH, C, D, C * D, D,
+                                        scale, int(causal), cur.cuda_stream), "ffa_bwd_dkdv_acc")
+        cur.wait_stream(side)
 
 
 # --------------------------------------------------------------------------- comm
@@ -165,7 +170,9 @@ class RingState:
 def ring_forward(q, k, v, state: RingState, scale: float, ops) -> tuple[torch.Tensor, torch.Tensor]:
     """Causal ring attention forward on this rank's zig-zag shard.
 
-    q, k, v: [B, H, 2C, D] bf16.  Returns (o [B, H, 2C, D] bf16, lse [B*H, 2C] fp32 base 2)."""
+    q, k, v: [B, H, 2C, D] bf16.  Returns (o [B, H, 2C, D] bf16, lse [B*H, 2C] fp32 base 2).
+    Each block's result is folded into an fp32 running output in a fixed order (step t,
+    then key chunk), so the output is rounded to bf16 once, at the end."""
     B, H, S2, D = q.shape
     r, P = state.rank, state.world
     qc = _chunks(q)
@@ -183,8 +190,8 @@ def ring_forward(q, k, v, state: RingState, scale: float, ops) -> tuple[torch.Te
                 kind = block_kind(my_ids[xi], kv_ids[yi])
                 if kind is None:
                     continue
-                o, lse = ops.fwd(qc[xi], kv[yi], kv[2 + yi], kind == "causal", scale)
-                ops.merge(acc[xi], acc_lse[xi], o, lse, not started[xi])
+                ops.fwd_merge(qc[xi], kv[yi], kv[2 + yi], kind == "causal", scale, acc[xi], acc_lse[xi],
+                              not started[xi])
                 started[xi] = True
         if pending is not None:
             kv = pending()
@@ -193,7 +200,14 @@ def ring_forward(q, k, v, state: RingState, scale: float, ops) -> tuple[torch.Te
 
 
 def ring_backward(q, k, v, o, lse, do, state: RingState, scale: float, ops):
-    """Deterministic ring backward; returns dq, dk, dv ([B, H, 2C, D], dtype of q)."""
+    """Deterministic ring backward; returns dq, dk, dv ([B, H, 2C, D], dtype of q).
+
+    Every block adds its gradients in fp32 into accumulators: dQ locally, dK/dV into the
+    accumulators that travel with their K/V chunk.  A chunk's accumulators leave for the
+    next rank as soon as this rank's blocks of the step are done, and their transfer
+    overlaps the next step's blocks (they are needed again only one step later, by the
+    next rank).  The order of the additions is fixed by the ring, so the result is
+    bitwise reproducible."""
     B, H, S2, D = q.shape
     r, P = state.rank, state.world
     qc, oc, doc = _chunks(q), _chunks(o), _chunks(do)
@@ -204,28 +218,30 @@ def ring_backward(q, k, v, o, lse, do, state: RingState, scale: float, ops):
     kv = list(_chunks(k)) + list(_chunks(v))
     dq = [torch.zeros(qc[0].shape, device=q.device, dtype=torch.float32) for _ in range(2)]
     dkv = [torch.zeros(qc[0].shape, device=q.device, dtype=torch.float32) for _ in range(4)]  # dk_a, dk_b, dv_a, dv_b
+    pending_dkv = None
     for t in range(P):
         src = (r - t) % P
         kv_ids = chunk_ids(src, P)
         # next step's K/V do not depend on this step: their transfer overlaps the blocks
         pending_kv = state.exchange.post(kv) if t + 1 < P else None
+        if pending_dkv is not None:
+            dkv = pending_dkv()  # the accumulators of the chunk this step's K/V belong to
         for xi in range(2):
             for yi in range(2):
                 kind = block_kind(my_ids[xi], kv_ids[yi])
                 if kind is None:
                     continue
-                gq, gk, gv = ops.bwd(qc[xi], kv[yi], kv[2 + yi], doc[xi], lse_c[xi], delta[xi], kind == "causal",
-                                     scale)
-                dq[xi] += gq.float()
-                dkv[yi] += gk.float()
-                dkv[2 + yi] += gv.float()
+                ops.bwd_acc(qc[xi], kv[yi], kv[2 + yi], doc[xi], lse_c[xi], delta[xi], kind == "causal", scale,
+                            dq[xi], dkv[yi], dkv[2 + yi])
         if P == 1:
             break
         # the dK/dV accumulators go to rank + 1 after every step; after the last step
         # they arrive back at the rank that owns them
-        dkv = state.exchange.post(dkv)()
+        pending_dkv = state.exchange.post(dkv)
         if pending_kv is not None:
             kv = pending_kv()
+    if pending_dkv is not None:
+        dkv = pending_dkv()
     dtype = q.dtype
     return (_unchunks(dq[0].to(dtype), dq[1].to(dtype), B, H), _unchunks(dkv[0].to(dtype), dkv[1].to(dtype), B, H),
             _unchunks(dkv[2].to(dtype), dkv[3].to(dtype), B, H))

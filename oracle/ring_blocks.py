@@ -2,8 +2,9 @@
 
 Implements the ``BlockOps`` interface of ``fastflashattention_b200.ring`` in plain torch
 fp32 with the same base-2 LSE convention as the kernels (reference
-``fastflash_attention/_kernel.py:274-279``): block forward with LSE, LSE merge, delta =
-rowsum(O*dO), and the block backward from the global LSE/delta
+``fastflash_attention/_kernel.py:274-279``): block forward merged into an fp32 running
+result by its LSE, delta = rowsum(O*dO), and the block backward from the global LSE/delta
+added into fp32 accumulators
 (``_kernel.py:379-448, 487-564``).  Used only by tests to check the ring's schedule,
 masking, merge and accumulation order on CPU ranks.
 """
@@ -23,7 +24,7 @@ def _scores(q, k, causal, scale):
 
 
 class CpuBlockOps:
-    def fwd(self, q, k, v, causal, scale):
+    def _fwd(self, q, k, v, causal, scale):
         s = _scores(q, k, causal, scale)
         m = s.amax(dim=-1, keepdim=True)
         l = torch.exp2(s - m).sum(dim=-1, keepdim=True)
@@ -31,23 +32,25 @@ class CpuBlockOps:
         p = torch.exp2(s - lse)
         return p @ v.float(), lse[..., 0]
 
-    def merge(self, acc, acc_lse, o, lse, first):
+    def fwd_merge(self, q, k, v, causal, scale, acc, acc_lse, first):
+        o, lse = self._fwd(q, k, v, causal, scale)
         if first:
             acc.copy_(o)
             acc_lse.copy_(lse)
             return
         m = torch.maximum(acc_lse, lse)
         wa, wb = torch.exp2(acc_lse - m), torch.exp2(lse - m)
-        acc.copy_((wa[..., None] * acc + wb[..., None] * o.float()) / (wa + wb)[..., None])
+        acc.copy_((wa[..., None] * acc + wb[..., None] * o) / (wa + wb)[..., None])
         acc_lse.copy_(m + torch.log2(wa + wb))
 
     def delta(self, o, do):
         return (o.float() * do.float()).sum(dim=-1)
 
-    def bwd(self, q, k, v, do, lse, delta, causal, scale):
+    def bwd_acc(self, q, k, v, do, lse, delta, causal, scale, dq_acc, dk_acc, dv_acc):
         s = _scores(q, k, causal, scale)
         p = torch.exp2(s - lse[..., None])
-        dv = p.transpose(-1, -2) @ do.float()
+        dv_acc += p.transpose(-1, -2) @ do.float()
         dp = do.float() @ v.float().transpose(-1, -2)
         ds = p * (dp - delta[..., None])
-        return ds @ k.float() * scale, ds.transpose(-1, -2) @ q.float() * scale, dv
+        dq_acc += ds @ k.float() * scale
+        dk_acc += ds.transpose(-1, -2) @ q.float() * scale
