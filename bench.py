@@ -555,6 +555,27 @@ def run_ring(args, rank, world, local_rank):
     return 0
 
 
+def run_once(args):
+    """A plain forward + backward of the library at --B --H --S --D causal, --warmup then
+    --steps times, with no timing: the command profilers wrap (ncu launch lists and
+    single-kernel captures on a case small enough to capture)."""
+    import torch
+    sys.path.insert(0, str(ROOT))
+    from fastflashattention_b200 import _lib, fast_attention
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v, do = (torch.randn(args.B, args.H, args.S, args.D, device="cuda", dtype=torch.bfloat16, generator=gen)
+                   for _ in range(4))
+    qg, kg, vg = (t.requires_grad_(True) for t in (q, k, v))
+    for _ in range(args.warmup + args.steps):
+        o = fast_attention(qg, kg, vg, is_causal=not args.noncausal)
+        torch.autograd.grad(o, (qg, kg, vg), do)
+    torch.cuda.synchronize()
+    print(json.dumps({"mode": "once", "B": args.B, "H": args.H, "S": args.S, "D": args.D,
+                      "causal": not args.noncausal, "device_status": list(_lib.device_status())}))
+    return 0
+
+
 # ------------------------------------------------------------------ comparator sweep
 SWEEP_S = [512, 1024, 2048, 4096, 8192, 16384]
 
@@ -737,11 +758,13 @@ def main():
     ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks (streams) of the pipelined e2e step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-box", action="store_true", help="skip the B8 H32 global-problem (configs[3]) figure")
-    ap.add_argument("--mode", choices=["shard", "ring", "sweep", "mem", "mem-worker"], default="shard",
+    ap.add_argument("--noncausal", action="store_true", help="--mode once: no causal mask")
+    ap.add_argument("--mode", choices=["shard", "ring", "sweep", "mem", "mem-worker", "once"], default="shard",
                     help="shard: batch x head data parallel (default workload); ring: context-parallel ring "
                          "over the sequence (BASELINE configs[4]: B1 H32 S131072 D128); sweep: fwd/bwd/step "
                          "of this library beside cuDNN SDPA, FlashAttention-2 and the reference's Triton "
-                         "kernels over S (one GPU); mem: peak memory of the same, fresh process per point")
+                         "kernels over S (one GPU); mem: peak memory of the same, fresh process per point; "
+                         "once: untimed fwd+bwd at the given shape (for profilers)")
     ap.add_argument("--sweep-s", default="", help="comma-separated S list for --mode sweep/mem")
     ap.add_argument("--sweep-blocks", default="", help="--mode sweep blocks, e.g. 128c,64n (default: all four)")
     ap.add_argument("--mem-impl", default="ours")
@@ -760,6 +783,8 @@ def main():
         return run_sweep(args)
     if args.mode == "mem":
         return run_mem(args)
+    if args.mode == "once":
+        return run_once(args)
     if args.mode == "mem-worker":
         return _mem_worker(args.mem_impl, args.S, args.mem_regime, args.B, args.H, args.D)
     if world > 1:

@@ -74,17 +74,15 @@ struct DkdvLayout {
 
 template <int D>
 struct DqLayout {
-  static constexpr int TILE = 128 * D * 2;  // Q, dO (resident) and K, V (streamed) tiles
-  static constexpr int K_STAGES = 3;        // K_j is read by S_j and, a step later, by dQ += dS_j K_j
-  static constexpr int V_STAGES = 2;        // V_j is read by dP_j only
-  static constexpr int Q_OFF = 0;
-  static constexpr int DO_OFF = TILE;
-  static constexpr int K_OFF = 2 * TILE;
+  static constexpr int TILE = 128 * D * 2;  // K, V (streamed) tiles; Q and dO live in TMEM
+  static constexpr int K_STAGES = 4;        // K_j is read by S_j and, a step later, by dQ += dS_j K_j
+  static constexpr int V_STAGES = 3;        // V_j is read by dP_j only
+  static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + K_STAGES * TILE;
   static constexpr int BAR_OFF = V_OFF + V_STAGES * TILE;
-  // qd_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], dp_full, dp_free,
+  // qd_ready, k_full[4], k_empty[4], v_full[3], v_empty[3], s_full, s_free, dp_full,
   // ds_ready, final, drain
-  static constexpr int NBARS = 1 + 2 * K_STAGES + 2 * V_STAGES + 2 + 5;
+  static constexpr int NBARS = 1 + 2 * K_STAGES + 2 * V_STAGES + 6;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
 };
@@ -549,36 +547,62 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
 // ====================================================================================
 // dQ
 // ====================================================================================
-// TMEM: S double buffer at columns 0 and 384, dP at 128, dQ at 256.
-__device__ __forceinline__ uint32_t dq_sbuf(int b) { return b ? 384u : 0u; }
+// TMEM (512 columns): S [0,128), dP [128,256), dQ [256,256+D), then Q and dO of the
+// block as packed bf16 (D/2 columns each): they are the A operands of S = Q K^T and
+// dP = dO V^T, so shared memory holds only the streamed K and V rings (4 + 3 slots).
+template <int D>
+struct DqTmem {
+  static constexpr uint32_t S = 0, DP = 128, DQ = 256, Q = 256 + D, DO = 256 + D + D / 2;
+};
+
+// Copy this thread's row of a [S, D] bf16 slice (row stride `stride_s` elements) into
+// D/2 packed TMEM columns starting at `taddr` (this warp's lanes); rows past the end
+// are zero.  Every lane of the warp calls it (tcgen05.st is warp-wide).
+template <int D>
+__device__ __forceinline__ void load_row_to_tmem(const __nv_bfloat16* __restrict__ src, bool valid, uint32_t taddr) {
+#pragma unroll
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t w[32];
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + 64 * c);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint4 x = valid ? __ldg(s4 + e) : make_uint4(0u, 0u, 0u, 0u);
+      w[4 * e + 0] = x.x;
+      w[4 * e + 1] = x.y;
+      w[4 * e + 2] = x.z;
+      w[4 * e + 3] = x.w;
+    }
+    tmem_st32(taddr + 32 * c, w);
+  }
+}
 
 // ACC: accumulate mode (ffa_bwd_dq_acc).
 template <int D, bool CAUSAL, bool ACC>
 __global__ void __launch_bounds__(bwd::NTHREADS, 1)
-    ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
-                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                      const __grid_constant__ CUtensorMap tm_dq,
-                      const float* __restrict__ LSE, const float* __restrict__ DELTA, float* __restrict__ DQ_ACC,
-                      int S, int BH, int group, long long stride_bh, long long stride_s, float scale_log2,
-                      float scale) {
+    ffa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_dq, const __nv_bfloat16* __restrict__ Qp,
+                      const __nv_bfloat16* __restrict__ DOp, const float* __restrict__ LSE,
+                      const float* __restrict__ DELTA, float* __restrict__ DQ_ACC, int S, int BH, int group,
+                      long long stride_bh, long long stride_s, float scale_log2, float scale) {
   using L = bwd::DqLayout<D>;
+  using T = DqTmem<D>;
   constexpr int SLABS = D / 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::BAR_OFF;
   constexpr int KS = L::K_STAGES, VS = L::V_STAGES;
-  const uint32_t qd_full = bar0;
+  const uint32_t qd_ready = bar0;
   auto k_full = [&](int s) { return bar0 + 8 * (1 + s); };
   auto k_empty = [&](int s) { return bar0 + 8 * (1 + KS + s); };
   auto v_full = [&](int s) { return bar0 + 8 * (1 + 2 * KS + s); };
   auto v_empty = [&](int s) { return bar0 + 8 * (1 + 2 * KS + VS + s); };
-  auto s_full = [&](int b) { return bar0 + 8 * (1 + 2 * KS + 2 * VS + b); };
-  const uint32_t dp_full = bar0 + 8 * (3 + 2 * KS + 2 * VS);
-  const uint32_t dp_free = dp_full + 8;
-  const uint32_t ds_ready = dp_full + 16;
-  const uint32_t final_bar = dp_full + 24;
-  const uint32_t drain_bar = dp_full + 32;
+  const uint32_t s_full = bar0 + 8 * (1 + 2 * KS + 2 * VS);
+  const uint32_t s_free = s_full + 8;
+  const uint32_t dp_full = s_full + 16;
+  const uint32_t ds_ready = s_full + 24;
+  const uint32_t final_bar = s_full + 32;
+  const uint32_t drain_bar = s_full + 40;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
@@ -593,7 +617,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   const int nk = CAUSAL ? min(nk_all, m0 / bwd::STEP + 1) : nk_all;
 
   if (threadIdx.x == 0) {
-    mbar_init(qd_full, 1);
+    mbar_init(qd_ready, 256);
     for (int s = 0; s < KS; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
@@ -602,10 +626,9 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    mbar_init(s_full(0), 1);
-    mbar_init(s_full(1), 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
     mbar_init(dp_full, 1);
-    mbar_init(dp_free, 256);
     mbar_init(ds_ready, 256);
     mbar_init(final_bar, 1);
     mbar_init(drain_bar, 1);
@@ -617,8 +640,6 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     tmem_relinquish();
   }
   if (warp == bwd::PRODUCER_WARP && lane == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
@@ -630,14 +651,9 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   if (warp >= 8) {
   setmaxnreg_dec<bwd::REGS_CONTROL>();
   if (warp == bwd::PRODUCER_WARP) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- producer: K, V rings
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      mbar_arrive_expect_tx(qd_full, 2 * L::TILE);
-      for (int sl = 0; sl < SLABS; ++sl) {
-        tma_load_3d(sbase + L::Q_OFF + sl * 16384, &tm_q, qd_full, sl * 64, m0, bh, keep);
-        tma_load_3d(sbase + L::DO_OFF + sl * 16384, &tm_do, qd_full, sl * 64, m0, bh, keep);
-      }
       int k_issued = 0, v_issued = 0;
       for (int j = 0; j < nk; ++j) {
         const int sk = j % KS, sv = j % VS;
@@ -655,7 +671,6 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         ++v_issued;
       }
       if (*abort_flag) {
-        mbar_wait_drain(qd_full, 0);
         for (int it = max(0, k_issued - KS); it < k_issued; ++it) mbar_wait_drain(k_full(it % KS), (it / KS) & 1);
         for (int it = max(0, v_issued - VS); it < v_issued; ++it) mbar_wait_drain(v_full(it % VS), (it / VS) & 1);
       }
@@ -663,83 +678,74 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   } else if (warp == bwd::MMA_WARP) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp runs the issue loop (its waits, descriptors and loop state are then
-    // warp-uniform) and one elected lane issues each group of MMAs and its commits.  On
-    // B200 this issues faster than a lane-0-only loop while the compute warps that share
-    // the warp's scheduler are busy (dQ 1.81 -> 1.46 ms at B4 H16 S8192 D128 causal).
+    // warp-uniform) and one elected lane issues each group of MMAs and its commits.
     {
       constexpr uint32_t IDESC_SD = idesc_bf16(128, bwd::STEP, false, false);  // [128 queries x 128 keys]
       constexpr uint32_t IDESC_G = idesc_bf16(128, D, false, true);            // [128 queries x D]
-      // Descriptors are built once per tile; a K-step only adds a constant.
-      const uint64_t qdesc = kmajor_desc(sbase + L::Q_OFF, 128, 0), dodesc = kmajor_desc(sbase + L::DO_OFF, 128, 0);
       auto k_addr = [&](int j) { return sbase + L::K_OFF + (j % KS) * L::TILE; };
       auto v_addr = [&](int j) { return sbase + L::V_OFF + (j % VS) * L::TILE; };
-      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into buffer j&1
+      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T  (Q from TMEM)
         if (!mbar_wait(k_full(j % KS), (j / KS) & 1, abort_flag, kErrDqMma)) return false;
-        FFA_BWD_TRACE(0, j);
         tc_fence_after();
-        const uint32_t d = tmem + dq_sbuf(j & 1);
         const uint64_t kd = kmajor_desc(k_addr(j), 128, 0);
         if (elect_one()) {
-          mma_ss(d, qdesc, kd, IDESC_SD, 0u);
+          mma_ts(tmem + T::S, tmem + T::Q, kd, IDESC_SD, 0u);
 #pragma unroll
           for (int ks = 1; ks < D / 16; ++ks)
-            mma_ss_acc(d, qdesc + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_SD);
-          mma_commit(s_full(j & 1));
+            mma_ts_acc(tmem + T::S, tmem + T::Q + 8 * ks, kd + kmajor_step(128, ks), IDESC_SD);
+          mma_commit(s_full);
         }
         __syncwarp();
-        FFA_BWD_TRACE(4, j);
         return true;
       };
-      auto issue_dp = [&](int j) -> bool {  // dP_j = dO V_j^T
+      auto issue_dp = [&](int j) -> bool {  // dP_j = dO V_j^T  (dO from TMEM)
         if (!mbar_wait(v_full(j % VS), (j / VS) & 1, abort_flag, kErrDqMma)) return false;
-        FFA_BWD_TRACE(1, j);
         tc_fence_after();
         const uint64_t vd = kmajor_desc(v_addr(j), 128, 0);
         if (elect_one()) {
-          mma_ss(tmem + 128, dodesc, vd, IDESC_SD, 0u);
+          mma_ts(tmem + T::DP, tmem + T::DO, vd, IDESC_SD, 0u);
 #pragma unroll
           for (int ks = 1; ks < D / 16; ++ks)
-            mma_ss_acc(tmem + 128, dodesc + kmajor_step(128, ks), vd + kmajor_step(128, ks), IDESC_SD);
+            mma_ts_acc(tmem + T::DP, tmem + T::DO + 8 * ks, vd + kmajor_step(128, ks), IDESC_SD);
           mma_commit(dp_full);
           mma_commit(v_empty(j % VS));
         }
         __syncwarp();
-        FFA_BWD_TRACE(5, j);
         return true;
       };
-      auto issue_g = [&](int j) -> bool {  // dQ += dS_j K_j
+      auto issue_g = [&](int j) -> bool {  // dQ += dS_j K_j  (dS_j packed in the dP columns)
         if (!mbar_wait(ds_ready, j & 1, abort_flag, kErrDqMma)) return false;
-        FFA_BWD_TRACE(2, j);
         tc_fence_after();
-        const uint32_t a = tmem + dq_sbuf(j & 1);
         const uint64_t kd = mnmajor_desc(k_addr(j), 128, 0);
         if (elect_one()) {
-          mma_ts(tmem + 256, a, kd, IDESC_G, j > 0 ? 1u : 0u);
+          mma_ts(tmem + T::DQ, tmem + T::DP, kd, IDESC_G, j > 0 ? 1u : 0u);
 #pragma unroll
           for (int ks = 1; ks < bwd::STEP / 16; ++ks)
-            mma_ts_acc(tmem + 256, bwd::packed_kstep_col(a, ks), kd + mnmajor_step(ks), IDESC_G);
+            mma_ts_acc(tmem + T::DQ, bwd::packed_kstep_col(tmem + T::DP, ks), kd + mnmajor_step(ks), IDESC_G);
           mma_commit(k_empty(j % KS));
         }
         __syncwarp();
-        FFA_BWD_TRACE(3, j);
         return true;
       };
-      bool ok = mbar_wait(qd_full, 0, abort_flag, kErrDqMma);
+      // Q and dO reach tensor memory through the compute warps
+      bool ok = mbar_wait(qd_ready, 0, abort_flag, kErrDqMma);
+      tc_fence_after();
       if (ok && nk > 0) {
         ok = issue_s(0);
         if (ok) ok = issue_dp(0);
       }
-      // S(j+1) and dP(j+1) run while the warpgroups turn step j into dS; dP(j+1) waits
-      // only until the warpgroups have copied dP(j) out of tensor memory.
+      // Per step: S(j+1) once the warpgroups hold S(j) in registers; dQ(j) once dS(j) is
+      // in the dP columns; then dP(j+1) over them (in order after dQ(j) has read dS(j)).
+      // The warpgroups exponentiate step j+1 while dQ(j) and dP(j+1) run, so the chain
+      // dQ(j) -> dP(j+1) -> dS(j+1) -> dQ(j+1) is shorter than a step's three MMAs.
       for (int j = 0; j < nk && ok; ++j) {
         if (j + 1 < nk) {
-          if (!(ok = issue_s(j + 1))) break;
-          if (!(ok = mbar_wait(dp_free, j & 1, abort_flag, kErrDqMma))) break;
-          FFA_BWD_TRACE(6, j + 1);
+          if (!(ok = mbar_wait(s_free, j & 1, abort_flag, kErrDqMma))) break;
           tc_fence_after();
-          if (!(ok = issue_dp(j + 1))) break;
+          if (!(ok = issue_s(j + 1))) break;
         }
         if (!(ok = issue_g(j))) break;
+        if (j + 1 < nk && !(ok = issue_dp(j + 1))) break;
       }
       // commits track the MMAs of the thread that issues them: the same elected lane
       if (elect_one()) {
@@ -759,30 +765,34 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
     const int qg = m0 + row;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const long long ridx = static_cast<long long>(bh) * S + qg;
+    {
+      // warpgroup 0 puts the block's Q rows into tensor memory, warpgroup 1 its dO rows
+      const __nv_bfloat16* src = (g ? DOp : Qp) + static_cast<long long>(bh) * stride_bh +
+                                 static_cast<long long>(qg < S ? qg : 0) * stride_s;
+      load_row_to_tmem<D>(src, qg < S, tmem + lane_off + (g ? T::DO : T::Q));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(qd_ready);
+    }
     const float lse = (qg < S) ? LSE[ridx] : INFINITY;
     const float dl = (qg < S) ? DELTA[ridx] : 0.f;
     const int lim = CAUSAL ? min(S - 1, qg) : S - 1;  // last visible key
+    const uint32_t t_s = tmem + lane_off + T::S + 64 * g;
+    const uint32_t t_dp = tmem + lane_off + T::DP + 64 * g;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
-      const int b = j & 1;
-      if (!(ok = mbar_wait(s_full(b), (j >> 1) & 1, abort_flag, kErrDqCompute))) break;
-      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, kErrDqCompute))) break;
-      if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(8 + 4 * g, j);
+      if (!(ok = mbar_wait(s_full, j & 1, abort_flag, kErrDqCompute))) break;
       tc_fence_after();
-      float sv[64], dp[64];
-      bwd::tmem_ld64(tmem + lane_off + dq_sbuf(b) + 64 * g, sv);
-      bwd::tmem_ld64(tmem + lane_off + 128 + 64 * g, dp);
+      float p[64];
+      bwd::tmem_ld64(t_s, p);
       tc_fence_before();
-      mbar_arrive(dp_free);
-      if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(9 + 4 * g, j);
+      mbar_arrive(s_free);  // S may now be overwritten by S(j+1)
       const int kc = j * bwd::STEP + 64 * g;  // first key of this thread's columns
       const bool need_mask = (kc + 64 > S) || (CAUSAL && kc + 63 > qg);
-      uint32_t dsp[32];
       const float2 c2 = make_float2(scale_log2, scale_log2), l2 = make_float2(-lse, -lse);
-      const float2 d2 = make_float2(dl, dl);
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
-        const float2 x = fma2(make_float2(sv[e], sv[e + 1]), c2, l2);
+        const float2 x = fma2(make_float2(p[e], p[e + 1]), c2, l2);
         float p0, p1;
         if (bwd::emu_group<D, false>(e >> 2)) {  // this pair on the FMA pipe
           const float2 ex = exp2_fma2(x);
@@ -796,24 +806,39 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           if (kc + e > lim) p0 = 0.f;
           if (kc + e + 1 > lim) p1 = 0.f;
         }
-        const float2 ds = mul2(make_float2(p0, p1), sub2(make_float2(dp[e], dp[e + 1]), d2));
+        p[e] = p0;
+        p[e + 1] = p1;
+      }
+      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, kErrDqCompute))) break;
+      tc_fence_after();
+      uint32_t dlo[32], dhi[32];
+      tmem_ld32(t_dp, dlo);
+      tmem_ld32(t_dp + 32, dhi);
+      tmem_ld_wait();
+      uint32_t dsp[32];
+      const float2 d2 = make_float2(dl, dl);
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) {
+        const uint32_t* src = (e < 32) ? dlo : dhi;
+        const int b = e & 31;
+        const float2 ds = mul2(make_float2(p[e], p[e + 1]),
+                               sub2(make_float2(__uint_as_float(src[b]), __uint_as_float(src[b + 1])), d2));
         dsp[e >> 1] = pack_bf16x2(ds.x, ds.y);
       }
-      if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(10 + 4 * g, j);
-      tmem_st32(tmem + lane_off + dq_sbuf(b) + 64 * g, dsp);
+      // dS(j) over the first half of this warpgroup's dP columns: the A operand of dQ(j)
+      tmem_st32(t_dp, dsp);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(ds_ready);
-      if ((threadIdx.x & 127) == 0) FFA_BWD_TRACE(11 + 4 * g, j);
     }
     const bool staged = ok && nk > 0 && mbar_wait(final_bar, 0, abort_flag, kErrDqCompute);
     constexpr bool acc_mode = ACC;
     if (staged) {
       tc_fence_after();
       if constexpr (acc_mode)  // fp32 accumulate: this CTA is the only writer of its query rows
-        bwd::add_acc_half<D>(tmem + lane_off + 256, g, DQ_ACC + ridx * D, qg < S, scale);
+        bwd::add_acc_half<D>(tmem + lane_off + T::DQ, g, DQ_ACC + ridx * D, qg < S, scale);
       else  // every MMA has finished: the K ring is free and holds the staged dQ tile
-        bwd::stage_acc_half<D>(tmem + lane_off + 256, g, sbase + L::K_OFF, row, scale);
+        bwd::stage_acc_half<D>(tmem + lane_off + T::DQ, g, sbase + L::K_OFF, row, scale);
     }
     const CUtensorMap* const maps[1] = {&tm_dq};
     bwd::store_staged<D, 1>(staged && !acc_mode, maps, sbase + L::K_OFF, m0, bh);
@@ -861,23 +886,21 @@ static int launch_dkdv_t(const BwdArgs& a, cudaStream_t stream) {
 template <int D, bool CAUSAL, bool ACC>
 static int launch_dq_t(const BwdArgs& a, cudaStream_t stream) {
   using LQ = bwd::DqLayout<D>;
-  CUtensorMap tq, tdo, tk, tv;
+  CUtensorMap tk, tv, tdq;
   int rc;
-  if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  if ((rc = make_tile_map(&tdo, a.dout, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tk, a.k, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
-  CUtensorMap tdq;
+  // accumulate mode stores nothing through this map: q serves as its base
   if ((rc = make_tile_map(&tdq, a.dq_acc ? a.q : a.dq, a.BH, a.S, D, a.stride_bh, a.stride_s, 128))) return rc;
   auto kern = ffa_bwd_dq_kernel<D, CAUSAL, ACC>;
   static unsigned long long configured = 0;
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), LQ::SMEM_BYTES, &configured))) return rc;
   if ((rc = check_launch_regs(reinterpret_cast<const void*>(kern), bwd::LAUNCH_REGS_NEEDED))) return rc;
   const dim3 grid(static_cast<unsigned>((a.S + bwd::LANES - 1) / bwd::LANES) * static_cast<unsigned>(a.BH));
-  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(tq, tdo, tk, tv, tdq, a.lse, a.delta, a.dq_acc, a.S, a.BH,
-                                                        work_group(a.BH, a.S, D, CAUSAL), a.stride_bh,
-                                                        a.stride_s, static_cast<float>(a.scale * kLog2e),
-                                                        static_cast<float>(a.scale));
+  kern<<<grid, bwd::NTHREADS, LQ::SMEM_BYTES, stream>>>(
+      tk, tv, tdq, static_cast<const __nv_bfloat16*>(a.q), static_cast<const __nv_bfloat16*>(a.dout), a.lse, a.delta,
+      a.dq_acc, a.S, a.BH, work_group(a.BH, a.S, D, CAUSAL), a.stride_bh, a.stride_s,
+      static_cast<float>(a.scale * kLog2e), static_cast<float>(a.scale));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FFA_ERR_LAUNCH, cudaGetErrorString(e));
   return FFA_OK;
