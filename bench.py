@@ -770,7 +770,7 @@ def main():
     ap.add_argument("--mem-impl", default="ours")
     ap.add_argument("--mem-regime", choices=["fwd", "train"], default="train")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and args.mode != "once":
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -23,9 +23,10 @@
 //   warp  9    MMA issuer (the whole warp runs the loop, an elected lane issues)
 // P and dS are written back to tensor memory as packed bf16 and feed the gradient MMAs
 // from there.  In the dq kernel dS overwrites the S columns it came from (warpgroup g's
-// 64 values land in [64g, 64g+32)).  In the dkdv kernel P(i) overwrites the first half of
-// the warpgroup's S columns as soon as it is computed (dV(i) then runs without waiting for
-// dP(i)) and dS(i) the first half of its dP columns.
+// 64 values land in [64g, 64g+32)).  In the dkdv kernel P and dS both go into the dP
+// columns once dP is in registers (warpgroup g: P at [64g, 64g+32), dS at
+// [64g+32, 64g+64) of the dP region), which frees the S columns for the next step's
+// S = K Q^T while this step's softmax is still running.
 #pragma once
 #include "ffa_common.cuh"
 
@@ -64,8 +65,8 @@ struct DkdvLayout {
   static constexpr int DO_STAGE_BYTES = TILE + 2 * STEP * 4;  // dO tile, lse[128], delta[128]
   static constexpr int BAR_OFF = DO_OFF + DO_STAGES * DO_STAGE_BYTES;
   // kv_full, q_full[3], q_empty[3], do_full[2], do_empty[2], s_full, dp_full, p_ready,
-  // ds_ready, final, drain
-  static constexpr int NBARS = 1 + 2 * Q_STAGES + 2 * DO_STAGES + 6;
+  // ds_ready, final, drain, s_free
+  static constexpr int NBARS = 1 + 2 * Q_STAGES + 2 * DO_STAGES + 7;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
   // no alignment slack: the kernel declares its dynamic shared memory 1024-byte aligned
   // (and checks it), which is what lets this layout fit in 227 KB
@@ -222,6 +223,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
   const uint32_t ds_ready = s_full + 24;
   const uint32_t final_bar = s_full + 32;
   const uint32_t drain_bar = s_full + 40;
+  const uint32_t s_free = s_full + 48;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
   auto q_addr = [&](int i) { return sbase + L::Q_OFF + (i % QS) * L::TILE; };
@@ -251,6 +253,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       mbar_init(do_empty(s), 1);
     }
     mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
     mbar_init(dp_full, 1);
     mbar_init(p_ready, 256);
     mbar_init(ds_ready, 256);
@@ -367,28 +370,28 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         __syncwarp();
         return true;
       };
-      auto issue_dv = [&](int i) -> bool {  // dV += P^T dO_i  (P_i packed in the S columns)
+      auto issue_dv = [&](int i) -> bool {  // dV += P^T dO_i
         if (!mbar_wait(p_ready, i & 1, abort_flag, kErrBwdMma)) return false;
         tc_fence_after();
         const uint64_t dd = mnmajor_desc(do_addr(i), 128, 0);
         if (elect_one()) {
-          mma_ts(tmem + 256, tmem, dd, IDESC_G, i > 0 ? 1u : 0u);
+          mma_ts(tmem + 256, tmem + 128, dd, IDESC_G, i > 0 ? 1u : 0u);
 #pragma unroll
           for (int ks = 1; ks < bwd::STEP / 16; ++ks)
-            mma_ts_acc(tmem + 256, bwd::packed_kstep_col(tmem, ks), dd + mnmajor_step(ks), IDESC_G);
+            mma_ts_acc(tmem + 256, bwd::packed_kstep_col(tmem + 128, ks), dd + mnmajor_step(ks), IDESC_G);
         }
         __syncwarp();
         return true;
       };
-      auto issue_dk = [&](int i) -> bool {  // dK += dS^T Q_i  (dS_i packed in the dP columns)
+      auto issue_dk = [&](int i) -> bool {  // dK += dS^T Q_i
         if (!mbar_wait(ds_ready, i & 1, abort_flag, kErrBwdMma)) return false;
         tc_fence_after();
         const uint64_t qd = mnmajor_desc(q_addr(i), 128, 0);
         if (elect_one()) {
-          mma_ts(tmem + 384, tmem + 128, qd, IDESC_G, i > 0 ? 1u : 0u);
+          mma_ts(tmem + 384, tmem + 128 + 32, qd, IDESC_G, i > 0 ? 1u : 0u);
 #pragma unroll
           for (int ks = 1; ks < bwd::STEP / 16; ++ks)
-            mma_ts_acc(tmem + 384, bwd::packed_kstep_col(tmem + 128, ks), qd + mnmajor_step(ks), IDESC_G);
+            mma_ts_acc(tmem + 384, bwd::packed_kstep_col(tmem + 128 + 32, ks), qd + mnmajor_step(ks), IDESC_G);
           mma_commit(q_empty(i % QS));
           mma_commit(do_empty(i % DS));
         }
@@ -400,17 +403,18 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
         ok = issue_s(0);
         if (ok) ok = issue_dp(0);
       }
-      // Per step: dV(i) as soon as P(i) is in the S columns, then S(i+1) over them (the
-      // tensor pipe runs one thread's MMAs in order, so dV(i) has read P(i) first), then
-      // dK(i) once dS(i) is in the dP columns, then dP(i+1) over those.  P(i) depends only
-      // on S(i), so the compute warps exponentiate step i+1 while dK(i) and dP(i+1) run,
-      // and the chain dK(i) -> dP(i+1) -> dS(i+1) -> dK(i+1) is shorter than a step's
-      // four MMAs: the tensor pipe, not the handoffs, sets the pace.
+      // S(i+1) as soon as the warpgroups have copied S(i) into registers, then dV(i),
+      // dK(i) and dP(i+1): P(i) and dS(i) live in the dP columns, so the next step's
+      // scores are computed during this step's whole softmax.
       for (int i = 0; i < nq && ok; ++i) {
         FFA_BWD_TRACE(0, i);
-        if (!(ok = issue_dv(i))) break;
+        if (i + 1 < nq) {
+          if (!(ok = mbar_wait(s_free, i & 1, abort_flag, kErrBwdMma))) break;
+          tc_fence_after();
+          if (!(ok = issue_s(i + 1))) break;
+        }
         FFA_BWD_TRACE(1, i);
-        if (i + 1 < nq && !(ok = issue_s(i + 1))) break;
+        if (!(ok = issue_dv(i))) break;
         FFA_BWD_TRACE(2, i);
         if (!(ok = issue_dk(i))) break;
         FFA_BWD_TRACE(3, i);
@@ -448,6 +452,8 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
       if (threadIdx.x == 0) FFA_BWD_TRACE(8, i);
       tc_fence_after();
       bwd::tmem_ld64(t_s, p);
+      tc_fence_before();
+      mbar_arrive(s_free);  // S may now be overwritten by S(i+1)
       if (threadIdx.x == 0) FFA_BWD_TRACE(12, i);
       uint32_t pk[32];
       {
@@ -479,20 +485,23 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           pk[e / 2 + 1] = pack_bf16x2(p[e + 2], p[e + 3]);
         }
       }
-      // P(i) over the first half of this warpgroup's S columns: the A operand of dV(i)
-      tmem_st32(t_s, pk);
-      tmem_st_wait();
-      tc_fence_before();
       if (threadIdx.x == 0) FFA_BWD_TRACE(14, i);
-      mbar_arrive(p_ready);
       if (!(ok = mbar_wait(dp_full, i & 1, abort_flag, kErrBwdCompute))) break;
       if (threadIdx.x == 0) FFA_BWD_TRACE(10, i);
       tc_fence_after();
+      // dP(i) comes into registers half by half; its columns then take P(i) (first half)
+      // and dS(i) (second half), so at most P, packed P and 32 dP values are live at once
       uint32_t dlo[32], dhi[32];
       tmem_ld32(t_dp, dlo);
+      tmem_ld_wait();
+      tmem_st32(t_dp, pk);
       tmem_ld32(t_dp + 32, dhi);
       tmem_ld_wait();
+      tmem_st_wait();
       if (threadIdx.x == 0) FFA_BWD_TRACE(13, i);
+      tc_fence_before();
+      if (threadIdx.x == 0) FFA_BWD_TRACE(9, i);
+      mbar_arrive(p_ready);
       {
         uint32_t dk[32];
 #pragma unroll
@@ -509,8 +518,7 @@ __global__ void __launch_bounds__(bwd::NTHREADS, 1)
           dk[e / 2] = pack_bf16x2(da.x, da.y);
           dk[e / 2 + 1] = pack_bf16x2(db.x, db.y);
         }
-        // dS(i) over the first half of this warpgroup's dP columns: the A operand of dK(i)
-        tmem_st32(t_dp, dk);
+        tmem_st32(t_dp + 32, dk);
         tmem_st_wait();
       }
       tc_fence_before();
