@@ -24,7 +24,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from ._kernel import fastflash_attn, fastflash_attn_train, FastFlashAttn, LOG2E  # noqa: F401
+from ._kernel import attention_train, fastflash_attn, fastflash_attn_train, FastFlashAttn, LOG2E  # noqa: F401
 
 __all__ = [
     "fast_attention",
@@ -106,7 +106,7 @@ def fast_attention(query, key, value, attn_mask=None, dropout_p=0.0,
         raise UnsupportedConfig(reason)
     wants_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (query, key, value))
     if wants_grad:
-        return fastflash_attn_train(query, key, value, is_causal, scale)
+        return attention_train(query, key, value, is_causal, scale)
     return fastflash_attn(query, key, value, is_causal, scale=scale)
 
 

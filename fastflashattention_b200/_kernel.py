@@ -6,53 +6,26 @@ Mirrors the reference module ``fastflash_attention/_kernel.py``:
   * ``fastflash_attn_train(q, k, v, causal, scale=None)``                 (:909-911)
   * ``LOG2E``                                                             (:40)
 with the Triton kernels replaced by calls into ``libffa_sm100.so`` (``include/ffa.h``).
-Outputs are allocated by the torch caching allocator on the inputs' device and every
-launch goes on the current torch CUDA stream.  Inputs are made contiguous first, as
-the reference does (:294, :791).  Head dims below 64 are zero-padded to 64 for the
-kernels (padding q/k with zeros leaves q.k unchanged and padded v columns are dropped),
-while the softmax scale keeps using the true head dim.
+``attention_train`` is the same differentiable attention as ``FastFlashAttn`` with its
+autograd node in C++; ``fast_attention`` uses it.
+The host work (contiguous inputs as the reference makes them, :294, :791; zero-padding of
+head dims below 64, which leaves q.k unchanged and drops the padded v columns while the
+softmax scale keeps the true head dim; output allocation by the torch caching allocator on
+the inputs' device; the launch on the current stream) runs in C++ as the torch operators
+``torch.ops.ffa_b200.*`` of ``libffa_torch.so`` (csrc/ffa_torch.cpp), over the C ABI.
 """
 from __future__ import annotations
 
-import contextlib
-
 import torch
-import torch.nn.functional as F
 from torch.autograd.function import once_differentiable
 
 from . import _lib
 
 LOG2E = 1.4426950408889634  # 1/ln(2): exp(x) = exp2(x*log2e)
 
-_KERNEL_DIMS = (64, 128)
-
 
 def _default_scale(head_dim: int) -> float:
     return 1.0 / (head_dim ** 0.5)
-
-
-def _kdim(d: int) -> int:
-    return 64 if d <= 64 else 128
-
-
-def _prep(t: torch.Tensor, kd: int) -> torch.Tensor:
-    """[B,H,S,D] -> contiguous [B*H,S,kd] (zero-padded along D when D < kd)."""
-    B, H, S, D = t.shape
-    t = t.contiguous()
-    if D != kd:
-        t = F.pad(t, (0, kd - D))
-    return t.reshape(B * H, S, kd)
-
-
-def _stream_ptr(dev: torch.device) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
-
-
-def _on_device(dev: torch.device):
-    """Context that makes `dev` current for the launch (a no-op when it already is)."""
-    if dev.index is None or dev.index == torch.cuda.current_device():
-        return contextlib.nullcontext()
-    return torch.cuda.device(dev)
 
 
 def fastflash_attn(q, k, v, causal: bool, return_lse: bool = False, scale=None):
@@ -64,51 +37,22 @@ def fastflash_attn(q, k, v, causal: bool, return_lse: bool = False, scale=None):
     B, H, S, D = q.shape
     assert D <= 128 and (D & (D - 1)) == 0, "HEAD_DIM must be a power of two <= 128"
     assert q.is_cuda and k.is_cuda and v.is_cuda
-    lib = _lib.load()
-    kd = _kdim(D)
-    qf, kf, vf = (_prep(t, kd) for t in (q, k, v))
-    o = torch.empty_like(qf)
-    lse = torch.empty(B * H, S, device=q.device, dtype=torch.float32) if return_lse else None
-    sm = _default_scale(D) if scale is None else float(scale)
-    with _on_device(q.device):
-        rc = lib.ffa_fwd(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), o.data_ptr(),
-                         lse.data_ptr() if lse is not None else None,
-                         B * H, S, kd, qf.stride(0), qf.stride(1), sm, int(bool(causal)),
-                         _stream_ptr(q.device))
-    _lib.check(rc, "ffa_fwd")
-    o = o.reshape(B, H, S, kd)
-    if kd != D:
-        o = o[..., :D].contiguous()
+    sc = None if scale is None else float(scale)
     if return_lse:
-        return o, lse.reshape(B, H, S)
-    return o
+        return _lib.ops().forward_lse(q, k, v, bool(causal), sc)
+    return _lib.ops().forward(q, k, v, bool(causal), sc)
 
 
 def _bwd(q, k, v, o, do, lse, causal: bool, scale):
     """dq, dk, dv for the saved forward state; all [B,H,S,D]."""
-    B, H, S, D = q.shape
-    lib = _lib.load()
-    kd = _kdim(D)
-    qf, kf, vf, of, dof = (_prep(t, kd) for t in (q, k, v, o, do))
-    lf = lse.reshape(B * H, S).contiguous()
-    dq = torch.empty_like(qf)
-    dk = torch.empty_like(kf)
-    dv = torch.empty_like(vf)
-    delta = torch.empty(B * H, S, device=q.device, dtype=torch.float32)
-    sm = _default_scale(D) if scale is None else float(scale)
-    with _on_device(q.device):
-        rc = lib.ffa_bwd(qf.data_ptr(), kf.data_ptr(), vf.data_ptr(), of.data_ptr(), dof.data_ptr(),
-                         lf.data_ptr(), delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
-                         B * H, S, kd, qf.stride(0), qf.stride(1), sm, int(bool(causal)),
-                         _stream_ptr(q.device))
-    _lib.check(rc, "ffa_bwd")
-    out = []
-    for g in (dq, dk, dv):
-        g = g.reshape(B, H, S, kd)
-        if kd != D:
-            g = g[..., :D].contiguous()
-        out.append(g)
-    return tuple(out)
+    return _lib.ops().backward(q, k, v, o, do, lse, bool(causal), None if scale is None else float(scale))
+
+
+def attention_train(q, k, v, causal: bool, scale=None):
+    """Differentiable attention through the C++ autograd node ``ffa_b200::attention``
+    (forward with LSE, saved q, k, v, o, lse, deterministic backward): the same work as
+    ``FastFlashAttn`` with no Python on the forward or backward path."""
+    return _lib.ops().attention(q, k, v, bool(causal), None if scale is None else float(scale))
 
 
 class FastFlashAttn(torch.autograd.Function):

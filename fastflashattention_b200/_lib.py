@@ -9,7 +9,7 @@ import ctypes
 import threading
 from pathlib import Path
 
-from .build import LIB_PATH
+from .build import LIB_PATH, TORCH_LIB_PATH
 
 FFA_OK = 0
 FFA_ERR_INVALID = 1
@@ -72,6 +72,28 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
         if path is None:
             _lib = lib
         return lib
+
+
+_ops_loaded = False
+_ops_lock = threading.Lock()
+
+
+def ops():
+    """The torch operators of ``libffa_torch.so`` (``torch.ops.ffa_b200``), loaded once.
+
+    They are the C++ host path (tensor preparation, launch on the current stream and the
+    autograd node) over the same C ABI; raises if the library is not built."""
+    global _ops_loaded
+    import torch
+    if not _ops_loaded:
+        load()  # the kernel library first (outside _ops_lock), so both bindings share one copy
+        with _ops_lock:
+            if not _ops_loaded:
+                if not TORCH_LIB_PATH.exists():
+                    raise ImportError(f"{TORCH_LIB_PATH.name} is not built; run `python -m fastflashattention_b200.build`")
+                torch.ops.load_library(str(TORCH_LIB_PATH))
+                _ops_loaded = True
+    return torch.ops.ffa_b200
 
 
 def last_error() -> str:

@@ -97,9 +97,15 @@ struct DqLayout {
 #ifndef FFA_BWD_EMU_D64
 #define FFA_BWD_EMU_D64 1
 #endif
+#ifndef FFA_BWD_EMU_DKDV_D128
+#define FFA_BWD_EMU_DKDV_D128 1
+#endif
+#ifndef FFA_BWD_EMU_DQ_D128
+#define FFA_BWD_EMU_DQ_D128 0
+#endif
 template <int D, bool DKDV>
 __device__ __forceinline__ constexpr bool emu_group(int g) {
-  return (g & 3) < (D == 64 ? FFA_BWD_EMU_D64 : (DKDV ? 1 : 0));
+  return (g & 3) < (D == 64 ? FFA_BWD_EMU_D64 : (DKDV ? FFA_BWD_EMU_DKDV_D128 : FFA_BWD_EMU_DQ_D128));
 }
 
 // TMEM column of the 16-deep K-step `ks` of a packed-bf16 A operand written by the two

@@ -28,6 +28,12 @@
 #pragma once
 #include "ffa_common.cuh"
 
+// Timeline hook for measurement builds (a clock read at fixed points of one CTA); expands
+// to nothing in the library.
+#ifndef FFA_FWD_TRACE
+#define FFA_FWD_TRACE(site, step)
+#endif
+
 namespace ffa {
 
 namespace fwd {
@@ -46,10 +52,17 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 // Of every 8 column pairs of an unmasked tile, how many are exponentiated on the FMA pipe
 // (packed polynomial) instead of MUFU.EX2.  At D=64 the MMAs take half as long, the
 // softmax bounds the kernel and 2 of 8 pairs gain 10-13 % (B200, B8 H16 D64).  At D=128,
-// with P handed over in halves, 1 of 8 pairs gains 1.1-1.6 % at B4 H16 causal S=8192 and
-// 16384 (three interleaved A/B runs); more pairs were slower.
+// 2 of 8 pairs measured 4 % faster than 1 of 8 at B4 H16 causal S=8192 (two interleaved
+// A/B rounds), and 3 of 8 about 2 %.  FFA_FWD_EMU_D128 / _D64 override the counts at build
+// time (measurement builds).
+#ifndef FFA_FWD_EMU_D128
+#define FFA_FWD_EMU_D128 2
+#endif
+#ifndef FFA_FWD_EMU_D64
+#define FFA_FWD_EMU_D64 2
+#endif
 template <int D>
-constexpr int emu_pairs() { return D == 64 ? 2 : 1; }
+constexpr int emu_pairs() { return D == 64 ? FFA_FWD_EMU_D64 : FFA_FWD_EMU_D128; }
 // Whether the two softmax warpgroups take turns on the exponentials.  At D=64 the MMAs
 // of a step take half as long, both warpgroups would otherwise exponentiate at the same
 // time, and taking turns is 5-6 % faster (B8 H16 S4096 D64); at D=128 it changes
@@ -281,9 +294,11 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         int sk = -1;
         uint32_t k_addr = 0;
         // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
+        FFA_FWD_TRACE(16, j);
         if (j < n_tiles0) {
           if (!(ok = issue_pv_tile(0, v_addr, j))) break;
         }
+        FFA_FWD_TRACE(17, j);
         if (next) {
           sk = it % fwd::STAGES;
           if (!(ok = mbar_wait(kv_full(sk), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
@@ -292,9 +307,11 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
           if (j + 1 < n_tiles0) issue_qk(0, k_addr);
         }
         // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
+        FFA_FWD_TRACE(18, j);
         if (j < n_tiles1) {
           if (!(ok = issue_pv_tile(1, v_addr, j))) break;
         }
+        FFA_FWD_TRACE(19, j);
         commit(kv_empty(sv));
         if (next) {
           if (j + 1 < n_tiles1) issue_qk(1, k_addr);
@@ -328,6 +345,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       if (!(ok = mbar_wait(s_full(i), j & 1, abort_flag, kErrFwdSoftmax))) break;
+      if (row == 0) FFA_FWD_TRACE(0 + 8 * i, j);
       tc_fence_after();
       float s[fwd::BN];
       {
@@ -359,6 +377,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         for (int c = 1; c < fwd::BN; ++c) a = fminf(a, s[c]);
         tmax = a * scale_log2;
       }
+      if (row == 0) FFA_FWD_TRACE(1 + 8 * i, j);
       const float m_new = fmaxf(m_used, tmax);
       const bool need = m_new > m_used + fwd::RESCALE_THRESHOLD;
       if (__any_sync(0xffffffffu, need)) {
@@ -418,6 +437,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
+        if (row == 0) FFA_FWD_TRACE(2 + h + 8 * i, j);
       };
       if (SEQ) {
         // take turns with the other warpgroup: wait for its exponentials of step j

@@ -444,8 +444,16 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
                   make_float2(0.2426111251115799f, 0.2426111251115799f));
   p = fma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
   p = fma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+#if FFA_EXP2_IMAD
+  // bits(p) + n * 2^23 as one integer multiply-add (FMA pipe) instead of shift + add (ALU)
+  uint32_t rx, ry;
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(rx) : "r"(__float_as_uint(t.x)), "r"(__float_as_uint(p.x)));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(ry) : "r"(__float_as_uint(t.y)), "r"(__float_as_uint(p.y)));
+  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
+#else
   return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+#endif
 }
 
 // Three-input max (sm_100 max.f32 with three sources).

@@ -64,3 +64,13 @@ def test_empty_problems_are_noops():
     assert lib.ffa_fwd(16, 16, 16, 16, None, 0, 128, 64, 8192, 64, 0.1, 1, None) == _lib.FFA_OK
     assert lib.ffa_fwd(16, 16, 16, 16, None, 4, 0, 128, 0, 128, 0.1, 0, None) == _lib.FFA_OK
     assert lib.ffa_lse_merge(16, 16, 16, 16, 0, 128, 1, None) == _lib.FFA_OK
+
+
+def test_torch_operators_load_and_register():
+    """The C++ host path (libffa_torch.so) loads on a machine without a GPU and registers
+    every operator the Python layer calls."""
+    from fastflashattention_b200.build import TORCH_LIB_PATH
+    assert TORCH_LIB_PATH.exists() and TORCH_LIB_PATH.parent.name == "fastflashattention_b200"
+    ops = _lib.ops()
+    for name in ("forward", "forward_lse", "backward", "attention"):
+        assert hasattr(ops, name), name
