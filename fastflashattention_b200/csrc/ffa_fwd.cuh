@@ -33,6 +33,9 @@
 #ifndef FFA_FWD_TRACE
 #define FFA_FWD_TRACE(site, step)
 #endif
+#ifndef FFA_FWD_CTA_TRACE
+#define FFA_FWD_CTA_TRACE(site, steps)
+#endif
 
 namespace ffa {
 
@@ -67,8 +70,11 @@ constexpr int emu_pairs() { return D == 64 ? FFA_FWD_EMU_D64 : FFA_FWD_EMU_D128;
 // of a step take half as long, both warpgroups would otherwise exponentiate at the same
 // time, and taking turns is 5-6 % faster (B8 H16 S4096 D64); at D=128 it changes
 // nothing measurable and stays off.
+#ifndef FFA_FWD_SEQ_D128
+#define FFA_FWD_SEQ_D128 0
+#endif
 template <int D>
-constexpr bool seq_turns() { return D == 64; }
+constexpr bool seq_turns() { return D == 64 || FFA_FWD_SEQ_D128; }
 
 template <int D>
 struct Layout {
@@ -149,6 +155,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   };
   const int n_tiles0 = tiles_for(m0), n_tiles1 = tiles_for(m0 + fwd::BM);
   const int n_kv = max(n_tiles0, n_tiles1);
+  FFA_FWD_CTA_TRACE(0, n_kv);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -524,6 +531,7 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  FFA_FWD_CTA_TRACE(1, n_kv);
 }
 
 // ------------------------------------------------------------------------------------
