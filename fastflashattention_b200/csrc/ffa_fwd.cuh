@@ -28,14 +28,6 @@
 #pragma once
 #include "ffa_common.cuh"
 
-// Timeline hook for measurement builds (a clock read at fixed points of one CTA); expands
-// to nothing in the library.
-#ifndef FFA_FWD_TRACE
-#define FFA_FWD_TRACE(site, step)
-#endif
-#ifndef FFA_FWD_CTA_TRACE
-#define FFA_FWD_CTA_TRACE(site, steps)
-#endif
 
 namespace ffa {
 
@@ -76,15 +68,15 @@ constexpr int emu_pairs() { return D == 64 ? FFA_FWD_EMU_D64 : FFA_FWD_EMU_D128;
 template <int D>
 constexpr bool seq_turns() { return D == 64 || FFA_FWD_SEQ_D128; }
 
-template <int D>
+template <int D, bool PERSIST>
 struct Layout {
   static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row bf16 tile
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = 2 * TILE_BYTES;
+  static constexpr int Q_OFF = 0;                 // Q tiles of a block (two buffers when persistent)
+  static constexpr int KV_OFF = (PERSIST ? 4 : 2) * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + STAGES * TILE_BYTES;
-  // barriers: q_full, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain,
-  // p_half[2], exp_done[2]
-  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2;
+  // barriers: q_full[0], kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_final[2], drain,
+  // p_half[2], exp_done[2], q_full[1], q_empty[2]
+  static constexpr int NBARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2 + 3;
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;  // + alignment slack
 };
@@ -115,19 +107,26 @@ __device__ __forceinline__ float row_max128(const float (&s)[fwd::BN]) {
 // MERGE: the ring's merge mode (ffa_fwd_merge); its epilogue folds the result into an
 // fp32 running result instead of storing bf16 O (a separate instantiation, so the plain
 // forward keeps its register allocation).
-template <int D, bool CAUSAL, bool MERGE, int EMU = fwd::emu_pairs<D>(), bool SEQ = fwd::seq_turns<D>()>
+// PERSIST: a CTA works through two blocks of one slice, the i-th and the last-but-i (equal
+// total work under a causal mask).  Q is double-buffered: the second block's Q tiles load
+// while the first runs, its first S = Q K^T is issued as soon as the first block's last
+// P.V is, and the first block's epilogue overlaps the second block's start, so the second
+// block pays little of the fixed cost of a CTA (launch, barrier and tensor-memory setup,
+// the first loads, the epilogue).
+template <int D, bool CAUSAL, bool MERGE, bool PERSIST, int EMU = fwd::emu_pairs<D>(),
+          bool SEQ = fwd::seq_turns<D>()>
 __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     ffa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                    float* __restrict__ LSE, int S, int BH, int group,
                    float scale_log2, float* __restrict__ ACC, float* __restrict__ ACC_LSE, int first) {
-  using L = fwd::Layout<D>;
+  static_assert(!(PERSIST && (SEQ || MERGE)), "the persistent forward runs without turn-taking or merge");
+  using L = fwd::Layout<D, PERSIST>;
   constexpr int SLABS = D / 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::BAR_OFF;
-  const uint32_t q_full = bar0;
   auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
   auto kv_empty = [&](int s) { return bar0 + 8 * (1 + fwd::STAGES + s); };
   auto s_full = [&](int i) { return bar0 + 8 * (1 + 2 * fwd::STAGES + i); };
@@ -136,29 +135,51 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
   const uint32_t drain_bar = bar0 + 8 * (7 + 2 * fwd::STAGES);
   auto p_half = [&](int i) { return bar0 + 8 * (8 + 2 * fwd::STAGES + i); };
   auto exp_done = [&](int i) { return bar0 + 8 * (10 + 2 * fwd::STAGES + i); };
+  // Q buffer b (b = block count & 1): q_full[b] when its tiles have landed, q_empty[b]
+  // when the block that used it has stored its output from it
+  auto q_full = [&](int b) { return b ? bar0 + 8 * (12 + 2 * fwd::STAGES) : bar0; };
+  auto q_empty = [&](int b) { return bar0 + 8 * (13 + 2 * fwd::STAGES + b); };
+  auto q_buf = [&](int b) { return sbase + L::Q_OFF + b * 2 * L::TILE_BYTES; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_mblk = (S + 2 * fwd::BM - 1) / (2 * fwd::BM);
-  const CtaWork work = cta_work(n_mblk, BH, group);
-  // heaviest causal blocks first
-  const int mblk = CAUSAL ? (n_mblk - 1 - work.rank) : work.rank;
-  const int bh = work.bh;
-  const int m0 = mblk * 2 * fwd::BM;
   const int n_kv_all = (S + fwd::BN - 1) / fwd::BN;
-  // number of key tiles each 128-row query tile visits (0 for a tile past the end)
-  auto tiles_for = [&](int mi) {
-    if (mi >= S) return 0;
-    return CAUSAL ? min(n_kv_all, (mi + fwd::BM - 1) / fwd::BN + 1) : n_kv_all;
+  // The n-th block of this CTA (rank < 0: none left).  One block per CTA, or (PERSIST) a
+  // pair of blocks of one slice whose ranks add up to n_mblk - 1: under a causal mask the
+  // pair's key tiles add up to the same count for every pair, so all CTAs carry equal work
+  // and the pairs of a group of slices still run together (their K/V stay in L2).
+  const int n_pairs = (n_mblk + 1) / 2;
+  auto item_of = [&](int n) -> CtaWork {
+    if (!PERSIST) return n == 0 ? cta_work(n_mblk, BH, group) : CtaWork{-1, 0};
+    const CtaWork w = cta_work(n_pairs, BH, group);
+    if (n == 0) return w;
+    if (n == 1 && n_mblk - 1 - w.rank != w.rank) return {n_mblk - 1 - w.rank, w.bh};
+    return {-1, 0};
   };
-  const int n_tiles0 = tiles_for(m0), n_tiles1 = tiles_for(m0 + fwd::BM);
-  const int n_kv = max(n_tiles0, n_tiles1);
-  FFA_FWD_CTA_TRACE(0, n_kv);
+  struct Item {
+    int bh, m0, nt0, nt1, n_kv;
+  };
+  auto decode = [&](CtaWork w) -> Item {
+    // heaviest causal blocks first
+    const int mblk = CAUSAL ? (n_mblk - 1 - w.rank) : w.rank;
+    const int m0 = mblk * 2 * fwd::BM;
+    // number of key tiles each 128-row query tile visits (0 for a tile past the end)
+    auto tiles_for = [&](int mi) {
+      if (mi >= S) return 0;
+      return CAUSAL ? min(n_kv_all, (mi + fwd::BM - 1) / fwd::BN + 1) : n_kv_all;
+    };
+    const int t0 = tiles_for(m0), t1 = tiles_for(m0 + fwd::BM);
+    return {w.bh, m0, t0, t1, max(t0, t1)};
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(q_full(b), 1);
+      mbar_init(q_empty(b), 2);
+    }
     for (int s = 0; s < fwd::STAGES; ++s) {
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
@@ -196,33 +217,43 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      mbar_arrive_expect_tx(q_full, 2 * L::TILE_BYTES);
-      for (int i = 0; i < 2; ++i)
-        for (int sl = 0; sl < SLABS; ++sl)
-          tma_load_3d(sbase + L::Q_OFF + i * L::TILE_BYTES + sl * 16384, &tm_q, q_full, sl * 64,
-                      m0 + i * fwd::BM, bh, keep);
-      int issued = 0;
+      int issued = 0, q_issued = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int which = 0; which < 2; ++which) {
-          const int it = 2 * j + which;
-          const int s = it % fwd::STAGES;
-          if (!mbar_wait(kv_empty(s), ((it / fwd::STAGES) & 1) ^ 1, abort_flag, kErrFwdProducer)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(kv_full(s), L::TILE_BYTES);
-          const CUtensorMap* tm = which ? &tm_v : &tm_k;
+      for (int n = 0; ok; ++n) {
+        const CtaWork cw = item_of(n);
+        if (cw.rank < 0) break;
+        const Item w = decode(cw);
+        const int b = n & 1;
+        // the block two back has stored its output out of this buffer
+        if (n >= 2 && !(ok = mbar_wait(q_empty(b), ((n >> 1) - 1) & 1, abort_flag, kErrFwdProducer))) break;
+        mbar_arrive_expect_tx(q_full(b), 2 * L::TILE_BYTES);
+        for (int i = 0; i < 2; ++i)
           for (int sl = 0; sl < SLABS; ++sl)
-            tma_load_3d(sbase + L::KV_OFF + s * L::TILE_BYTES + sl * 16384, tm, kv_full(s), sl * 64,
-                        j * fwd::BN, bh, keep);
-          ++issued;
+            tma_load_3d(q_buf(b) + i * L::TILE_BYTES + sl * 16384, &tm_q, q_full(b), sl * 64, w.m0 + i * fwd::BM,
+                        w.bh, keep);
+        ++q_issued;
+        for (int j = 0; j < w.n_kv && ok; ++j) {
+          for (int which = 0; which < 2; ++which) {
+            const int it = issued;
+            const int s = it % fwd::STAGES;
+            if (!mbar_wait(kv_empty(s), ((it / fwd::STAGES) & 1) ^ 1, abort_flag, kErrFwdProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(kv_full(s), L::TILE_BYTES);
+            const CUtensorMap* tm = which ? &tm_v : &tm_k;
+            for (int sl = 0; sl < SLABS; ++sl)
+              tma_load_3d(sbase + L::KV_OFF + s * L::TILE_BYTES + sl * 16384, tm, kv_full(s), sl * 64,
+                          j * fwd::BN, w.bh, keep);
+            ++issued;
+          }
         }
       }
-      if (!ok) {
+      if (*abort_flag) {
         // let in-flight copies land before the CTA's shared memory goes away
         for (int it = max(0, issued - fwd::STAGES); it < issued; ++it)
           mbar_wait_drain(kv_full(it % fwd::STAGES), (it / fwd::STAGES) & 1);
+        for (int n = max(0, q_issued - 2); n < q_issued; ++n) mbar_wait_drain(q_full(n & 1), (n >> 1) & 1);
       }
     }
   } else if (warp == fwd::MMA_WARP) {
@@ -232,103 +263,107 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     {
       constexpr uint32_t IDESC_QK = idesc_bf16(128, fwd::BN, false, false);
       constexpr uint32_t IDESC_PV = idesc_bf16(128, D, false, true);
-      const uint32_t q_addr0 = sbase + L::Q_OFF, q_addr1 = sbase + L::Q_OFF + L::TILE_BYTES;
-      bool ok = mbar_wait(q_full, 0, abort_flag, kErrFwdMma);
+      bool ok = true;
       int it = 0;
-      // Descriptors are built once per tile / stage; a K-step only adds a constant.
-      const uint64_t qdesc0 = kmajor_desc(q_addr0, 128, 0), qdesc1 = kmajor_desc(q_addr1, 128, 0);
-      auto issue_qk = [&](int i, uint32_t k_addr) {
-        const uint64_t qd = i ? qdesc1 : qdesc0;
-        const uint64_t kd = kmajor_desc(k_addr, 128, 0);
-        const uint32_t d = tmem + i * 128;
-        if (elect_one()) {
-          mma_ss(d, qd, kd, IDESC_QK, 0u);
-#pragma unroll
-          for (int ks = 1; ks < D / 16; ++ks)
-            mma_ss_acc(d, qd + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_QK);
-          mma_commit(s_full(i));
-        }
-        __syncwarp();
-      };
-      // K-steps [k0, k1) of O_i += P_i V_j (16 keys = 8 TMEM columns of packed P each)
-      auto issue_pv = [&](int i, uint32_t v_addr, int j, int k0, int k1) {
-        const uint64_t vd = mnmajor_desc(v_addr, fwd::BN, 0);
-        const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
-        if (elect_one()) {
-          for (int ks = k0; ks < k1; ++ks) {
-            if (ks == 0)
-              mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
-            else
-              mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
-          }
-        }
-        __syncwarp();
-      };
-      // P_i(j) V_j: in two halves when the softmax hands P over in halves
-      auto issue_pv_tile = [&](int i, uint32_t v_addr, int j) -> bool {
-        if (!mbar_wait(p_half(i), j & 1, abort_flag, kErrFwdMma)) return false;
-        tc_fence_after();
-        issue_pv(i, v_addr, j, 0, fwd::BN / 32);
-        if (!mbar_wait(p_ready(i), j & 1, abort_flag, kErrFwdMma)) return false;
-        tc_fence_after();
-        issue_pv(i, v_addr, j, fwd::BN / 32, fwd::BN / 16);
-        return true;
-      };
+      int steps[2] = {0, 0};  // P hand-overs of each tile so far (barrier phases)
       // commits track the MMAs of the thread that issues them: the same elected lane
       auto commit = [&](uint32_t bar) {
         if (elect_one()) mma_commit(bar);
         __syncwarp();
       };
-      // prologue: S_i(0)
-      if (ok && n_kv > 0) {
-        const int s = it % fwd::STAGES;
-        ok = mbar_wait(kv_full(s), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma);
-        if (ok) {
+      for (int n = 0; ok; ++n) {
+        const CtaWork cw = item_of(n);
+        if (cw.rank < 0) break;
+        const Item w = decode(cw);
+        const int b = n & 1;
+        if (!(ok = mbar_wait(q_full(b), (n >> 1) & 1, abort_flag, kErrFwdMma))) break;
+        // Descriptors are built once per tile / stage; a K-step only adds a constant.
+        const uint64_t qdesc0 = kmajor_desc(q_buf(b), 128, 0), qdesc1 = kmajor_desc(q_buf(b) + L::TILE_BYTES, 128, 0);
+        auto issue_qk = [&](int i, uint32_t k_addr) {
+          const uint64_t qd = i ? qdesc1 : qdesc0;
+          const uint64_t kd = kmajor_desc(k_addr, 128, 0);
+          const uint32_t d = tmem + i * 128;
+          if (elect_one()) {
+            mma_ss(d, qd, kd, IDESC_QK, 0u);
+#pragma unroll
+            for (int ks = 1; ks < D / 16; ++ks)
+              mma_ss_acc(d, qd + kmajor_step(128, ks), kd + kmajor_step(128, ks), IDESC_QK);
+            mma_commit(s_full(i));
+          }
+          __syncwarp();
+        };
+        // K-steps [k0, k1) of O_i += P_i V_j (16 keys = 8 TMEM columns of packed P each)
+        auto issue_pv = [&](int i, uint32_t v_addr, int j, int k0, int k1) {
+          const uint64_t vd = mnmajor_desc(v_addr, fwd::BN, 0);
+          const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
+          if (elect_one()) {
+            for (int ks = k0; ks < k1; ++ks) {
+              if (ks == 0)
+                mma_ts(d, a, vd, IDESC_PV, j > 0 ? 1u : 0u);
+              else
+                mma_ts_acc(d, a + ks * 8, vd + mnmajor_step(ks), IDESC_PV);
+            }
+          }
+          __syncwarp();
+        };
+        // P_i(j) V_j: in two halves when the softmax hands P over in halves
+        auto issue_pv_tile = [&](int i, uint32_t v_addr, int j) -> bool {
+          const int ph = (steps[i] + j) & 1;
+          if (!mbar_wait(p_half(i), ph, abort_flag, kErrFwdMma)) return false;
+          tc_fence_after();
+          issue_pv(i, v_addr, j, 0, fwd::BN / 32);
+          if (!mbar_wait(p_ready(i), ph, abort_flag, kErrFwdMma)) return false;
+          tc_fence_after();
+          issue_pv(i, v_addr, j, fwd::BN / 32, fwd::BN / 16);
+          return true;
+        };
+        // prologue: S_i(0)
+        if (w.n_kv > 0) {
+          const int s = it % fwd::STAGES;
+          if (!(ok = mbar_wait(kv_full(s), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
           tc_fence_after();
           const uint32_t k_addr = sbase + L::KV_OFF + s * L::TILE_BYTES;
-          if (n_tiles0 > 0) issue_qk(0, k_addr);
-          if (n_tiles1 > 0) issue_qk(1, k_addr);
+          if (w.nt0 > 0) issue_qk(0, k_addr);
+          if (w.nt1 > 0) issue_qk(1, k_addr);
           commit(kv_empty(s));
           ++it;
         }
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int sv = it % fwd::STAGES;
-        if (!(ok = mbar_wait(kv_full(sv), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
-        ++it;
-        const uint32_t v_addr = sbase + L::KV_OFF + sv * L::TILE_BYTES;
-        const bool next = (j + 1 < n_kv);
-        int sk = -1;
-        uint32_t k_addr = 0;
-        // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
-        FFA_FWD_TRACE(16, j);
-        if (j < n_tiles0) {
-          if (!(ok = issue_pv_tile(0, v_addr, j))) break;
-        }
-        FFA_FWD_TRACE(17, j);
-        if (next) {
-          sk = it % fwd::STAGES;
-          if (!(ok = mbar_wait(kv_full(sk), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
-          tc_fence_after();
-          k_addr = sbase + L::KV_OFF + sk * L::TILE_BYTES;
-          if (j + 1 < n_tiles0) issue_qk(0, k_addr);
-        }
-        // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
-        FFA_FWD_TRACE(18, j);
-        if (j < n_tiles1) {
-          if (!(ok = issue_pv_tile(1, v_addr, j))) break;
-        }
-        FFA_FWD_TRACE(19, j);
-        commit(kv_empty(sv));
-        if (next) {
-          if (j + 1 < n_tiles1) issue_qk(1, k_addr);
-          commit(kv_empty(sk));
+        for (int j = 0; j < w.n_kv && ok; ++j) {
+          const int sv = it % fwd::STAGES;
+          if (!(ok = mbar_wait(kv_full(sv), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
           ++it;
+          const uint32_t v_addr = sbase + L::KV_OFF + sv * L::TILE_BYTES;
+          const bool next = (j + 1 < w.n_kv);
+          int sk = -1;
+          uint32_t k_addr = 0;
+          // tile 0: O0 += P0 V_j, then S0 = Q0 K_{j+1}^T
+          if (j < w.nt0) {
+            if (!(ok = issue_pv_tile(0, v_addr, j))) break;
+          }
+          if (next) {
+            sk = it % fwd::STAGES;
+            if (!(ok = mbar_wait(kv_full(sk), (it / fwd::STAGES) & 1, abort_flag, kErrFwdMma))) break;
+            tc_fence_after();
+            k_addr = sbase + L::KV_OFF + sk * L::TILE_BYTES;
+            if (j + 1 < w.nt0) issue_qk(0, k_addr);
+          }
+          // tile 1: O1 += P1 V_j, then S1 = Q1 K_{j+1}^T
+          if (j < w.nt1) {
+            if (!(ok = issue_pv_tile(1, v_addr, j))) break;
+          }
+          commit(kv_empty(sv));
+          if (next) {
+            if (j + 1 < w.nt1) issue_qk(1, k_addr);
+            commit(kv_empty(sk));
+            ++it;
+          }
         }
-      }
-      if (ok) {
-        commit(o_final(0));
-        commit(o_final(1));
+        if (!ok) break;
+        // O_i complete (a tile with no keys gets no commit: its warpgroup does not wait)
+        if (w.nt0 > 0) commit(o_final(0));
+        if (w.nt1 > 0) commit(o_final(1));
+        steps[0] += w.nt0;
+        steps[1] += w.nt1;
       }
       // every issued MMA has finished before TMEM is released
       commit(drain_bar);
@@ -341,187 +376,198 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     // ------------------------------------------------------------------ softmax
     const int i = warp >> 2;            // tile
     const int row = (warp & 3) * 32 + lane;
-    const int mi = m0 + i * fwd::BM;
-    const int grow = mi + row;
-    const int nt = i ? n_tiles1 : n_tiles0;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + lane_off + i * 128;
     const uint32_t t_o = tmem + lane_off + 256 + i * 128;
-    float m_used = -INFINITY;
-    float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (!(ok = mbar_wait(s_full(i), j & 1, abort_flag, kErrFwdSoftmax))) break;
-      if (row == 0) FFA_FWD_TRACE(0 + 8 * i, j);
-      tc_fence_after();
-      float s[fwd::BN];
-      {
-        uint32_t r[4][32];
+    int steps = 0, finals = 0;  // this tile's S hand-overs and completed blocks (barrier phases)
+    for (int n = 0; ok; ++n) {
+      const CtaWork cw = item_of(n);
+      if (cw.rank < 0) break;
+      const Item w = decode(cw);
+      const int bh = w.bh;
+      const int mi = w.m0 + i * fwd::BM;
+      const int grow = mi + row;
+      const int nt = i ? w.nt1 : w.nt0;
+      float m_used = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < nt; ++j) {
+        if (!(ok = mbar_wait(s_full(i), (steps + j) & 1, abort_flag, kErrFwdSoftmax))) break;
+        tc_fence_after();
+        float s[fwd::BN];
+        {
+          uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
-        tmem_ld_wait();
+          for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r[c]);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]);
+            for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]);
+        }
+        const int n0 = j * fwd::BN;
+        const bool need_mask = (n0 + fwd::BN > S) || (CAUSAL && n0 + fwd::BN - 1 > mi);
+        // Row max of the scaled scores.  Unmasked tiles reduce the raw scores and scale
+        // once (scale*log2e > 0 keeps the order; a negative scale reduces with min);
+        // masked tiles (diagonal / ragged tail) scale first and drop masked columns.
+        float tmax;
+        if (need_mask) {
+          const int lim = CAUSAL ? min(S - 1, grow) : (S - 1);
+#pragma unroll
+          for (int c = 0; c < fwd::BN; ++c) s[c] = (n0 + c > lim) ? -INFINITY : s[c] * scale_log2;
+          tmax = row_max128(s);
+        } else if (scale_log2 >= 0.f) {
+          tmax = row_max128(s) * scale_log2;
+        } else {
+          float a = s[0];
+#pragma unroll
+          for (int c = 1; c < fwd::BN; ++c) a = fminf(a, s[c]);
+          tmax = a * scale_log2;
+        }
+        const float m_new = fmaxf(m_used, tmax);
+        const bool need = m_new > m_used + fwd::RESCALE_THRESHOLD;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_safe = (m_new == -INFINITY) ? 0.f : m_new;
+          const float alpha = fast_exp2(m_used - m_safe);
+          if (j > 0) {
+            // O_i(j-1) is complete: S_i(j) was committed after P_i(j-1) V_{j-1}.
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(t_o + c * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st32(t_o + c * 32, r);
+            }
+          }
+          l *= alpha;
+          m_used = m_new;
+        }
+        const float m_safe = (m_used == -INFINITY) ? 0.f : m_used;
+        uint32_t p[2][32];
+        float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 c2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m_safe, -m_safe);
+        // Column pairs [h*32, h*32+32) -> p[h] -> TMEM columns [h*32, h*32+32) of S_i.
+        auto half = [&](const int h) {
+          if (need_mask) {
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+              const int c = h * 32 + u;
+              const float p0 = fast_exp2(s[2 * c] - m_safe);
+              const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
+              sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
+              p[h][u] = pack_bf16x2(p0, p1);
+            }
+          } else {
+            // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+              const int c = h * 32 + u;
+              const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), c2, nm2);
+              float p0, p1;
+              if ((c & 7) < EMU) {
+                const float2 e2 = exp2_fma2(x);
+                p0 = e2.x;
+                p1 = e2.y;
+              } else {
+                p0 = fast_exp2(x.x);
+                p1 = fast_exp2(x.y);
+              }
+              sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
+              p[h][u] = pack_bf16x2(p0, p1);
+            }
+          }
+          if (SEQ && h == 1) mbar_arrive(exp_done(i));
+          tmem_st32(t_s + 32 * h, p[h]);
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
+        };
+        if (SEQ) {
+          // take turns with the other warpgroup: wait for its exponentials of step j
+          // (tile 1) or j-1 (tile 0), when it has such a step (one block per CTA here)
+          const int oj = i ? j : j - 1;
+          if (oj >= 0 && oj < (i ? w.nt0 : w.nt1) &&
+              !(ok = mbar_wait(exp_done(i ^ 1), oj & 1, abort_flag, kErrFwdSoftmax)))
+            break;
+        }
+        half(0);
+        half(1);
+        const float2 sv = add2(sum2[0], sum2[1]);
+        l += sv.x + sv.y;
       }
-      const int n0 = j * fwd::BN;
-      const bool need_mask = (n0 + fwd::BN > S) || (CAUSAL && n0 + fwd::BN - 1 > mi);
-      // Row max of the scaled scores.  Unmasked tiles reduce the raw scores and scale
-      // once (scale*log2e > 0 keeps the order; a negative scale reduces with min);
-      // masked tiles (diagonal / ragged tail) scale first and drop masked columns.
-      float tmax;
-      if (need_mask) {
-        const int lim = CAUSAL ? min(S - 1, grow) : (S - 1);
-#pragma unroll
-        for (int c = 0; c < fwd::BN; ++c) s[c] = (n0 + c > lim) ? -INFINITY : s[c] * scale_log2;
-        tmax = row_max128(s);
-      } else if (scale_log2 >= 0.f) {
-        tmax = row_max128(s) * scale_log2;
-      } else {
-        float a = s[0];
-#pragma unroll
-        for (int c = 1; c < fwd::BN; ++c) a = fminf(a, s[c]);
-        tmax = a * scale_log2;
-      }
-      if (row == 0) FFA_FWD_TRACE(1 + 8 * i, j);
-      const float m_new = fmaxf(m_used, tmax);
-      const bool need = m_new > m_used + fwd::RESCALE_THRESHOLD;
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_safe = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = fast_exp2(m_used - m_safe);
-        if (j > 0) {
-          // O_i(j-1) is complete: S_i(j) was committed after P_i(j-1) V_{j-1}.
+      steps += nt;
+      // Epilogue: O_i / l into its Q tile (free once every MMA of the block has finished),
+      // then one TMA store; rows at or past S are clipped by the tensor map.  Every thread
+      // of the warpgroup reaches the barrier, finished or not, so none can wait for one
+      // that left.
+      const bool staged = ok && nt > 0 && mbar_wait(o_final(i), finals & 1, abort_flag, kErrFwdSoftmax);
+      if (nt > 0) ++finals;
+      const uint32_t o_tile = q_buf(n & 1) + i * L::TILE_BYTES;
+      if constexpr (MERGE) {
+        // Merge mode: fold this result (O = acc/l, base-2 LSE lp) into the running fp32
+        // result of its rows: w_a = 2^(la - m), w_b = 2^(lp - m), m = max(la, lp);
+        // acc = (w_a acc + w_b O) / (w_a + w_b), acc_lse = m + log2(w_a + w_b).  This
+        // thread's row has no other writer in the launch.
+        if (staged) {
+          tc_fence_after();
+          const bool valid = grow < S;
+          const long long idx = static_cast<long long>(bh) * S + grow;
+          const float lp = (l == 0.f) ? -INFINITY : m_used + log2f(l);
+          const float la = (first || !valid) ? -INFINITY : ACC_LSE[idx];
+          const float mm = fmaxf(la, lp);
+          const float wa = (mm == -INFINITY) ? 1.f : exp2f(la - mm);
+          const float wb = (mm == -INFINITY) ? 0.f : exp2f(lp - mm);
+          const float inv = 1.f / (wa + wb);
+          const float ca = wa * inv, cb = (l == 0.f) ? 0.f : wb * inv / l;
+          float* dst = ACC + idx * D;
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(t_o + c * 32, r);
             tmem_ld_wait();
+            if (valid) {
+              float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st32(t_o + c * 32, r);
-          }
-        }
-        l *= alpha;
-        m_used = m_new;
-      }
-      const float m_safe = (m_used == -INFINITY) ? 0.f : m_used;
-      uint32_t p[2][32];
-      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 c2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-m_safe, -m_safe);
-      // Column pairs [h*32, h*32+32) -> p[h] -> TMEM columns [h*32, h*32+32) of S_i.
-      auto half = [&](const int h) {
-        if (need_mask) {
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int c = h * 32 + u;
-            const float p0 = fast_exp2(s[2 * c] - m_safe);
-            const float p1 = fast_exp2(s[2 * c + 1] - m_safe);
-            sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
-            p[h][u] = pack_bf16x2(p0, p1);
-          }
-        } else {
-          // EMU of every 8 column pairs take the FMA-pipe exp2, the rest MUFU.EX2
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const int c = h * 32 + u;
-            const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), c2, nm2);
-            float p0, p1;
-            if ((c & 7) < EMU) {
-              const float2 e2 = exp2_fma2(x);
-              p0 = e2.x;
-              p1 = e2.y;
-            } else {
-              p0 = fast_exp2(x.x);
-              p1 = fast_exp2(x.y);
+              for (int e = 0; e < 8; ++e) {
+                const float4 a = first ? make_float4(0.f, 0.f, 0.f, 0.f) : d4[e];
+                d4[e] = make_float4(fmaf(a.x, ca, __uint_as_float(r[4 * e + 0]) * cb),
+                                    fmaf(a.y, ca, __uint_as_float(r[4 * e + 1]) * cb),
+                                    fmaf(a.z, ca, __uint_as_float(r[4 * e + 2]) * cb),
+                                    fmaf(a.w, ca, __uint_as_float(r[4 * e + 3]) * cb));
+              }
             }
-            sum2[u & 1] = add2(sum2[u & 1], make_float2(p0, p1));
-            p[h][u] = pack_bf16x2(p0, p1);
           }
+          if (valid) ACC_LSE[idx] = (mm == -INFINITY) ? -INFINITY : mm + log2f(wa + wb);
         }
-        if (SEQ && h == 1) mbar_arrive(exp_done(i));
-        tmem_st32(t_s + 32 * h, p[h]);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(h == 0 ? p_half(i) : p_ready(i));
-        if (row == 0) FFA_FWD_TRACE(2 + h + 8 * i, j);
-      };
-      if (SEQ) {
-        // take turns with the other warpgroup: wait for its exponentials of step j
-        // (tile 1) or j-1 (tile 0), when it has such a step
-        const int oj = i ? j : j - 1;
-        if (oj >= 0 && oj < (i ? n_tiles0 : n_tiles1) &&
-            !(ok = mbar_wait(exp_done(i ^ 1), oj & 1, abort_flag, kErrFwdSoftmax)))
-          break;
-      }
-      half(0);
-      half(1);
-      const float2 sv = add2(sum2[0], sum2[1]);
-      l += sv.x + sv.y;
-    }
-    // Epilogue: O_i / l into its Q tile (free once every MMA of tile i has finished), then
-    // one TMA store; rows at or past S are clipped by the tensor map.  Every thread of the
-    // warpgroup reaches the barrier, finished or not, so none can wait for one that left.
-    const bool staged = ok && nt > 0 && mbar_wait(o_final(i), 0, abort_flag, kErrFwdSoftmax);
-    const uint32_t o_tile = sbase + L::Q_OFF + i * L::TILE_BYTES;
-    if constexpr (MERGE) {
-      // Merge mode: fold this result (O = acc/l, base-2 LSE lp) into the running fp32
-      // result of its rows: w_a = 2^(la - m), w_b = 2^(lp - m), m = max(la, lp);
-      // acc = (w_a acc + w_b O) / (w_a + w_b), acc_lse = m + log2(w_a + w_b).  This
-      // thread's row has no other writer in the launch.
-      if (staged) {
+      } else if (staged) {
         tc_fence_after();
-        const bool valid = grow < S;
-        const long long idx = static_cast<long long>(bh) * S + grow;
-        const float lp = (l == 0.f) ? -INFINITY : m_used + log2f(l);
-        const float la = (first || !valid) ? -INFINITY : ACC_LSE[idx];
-        const float mm = fmaxf(la, lp);
-        const float wa = (mm == -INFINITY) ? 1.f : exp2f(la - mm);
-        const float wb = (mm == -INFINITY) ? 0.f : exp2f(lp - mm);
-        const float inv = 1.f / (wa + wb);
-        const float ca = wa * inv, cb = (l == 0.f) ? 0.f : wb * inv / l;
-        float* dst = ACC + idx * D;
+        const float l_safe = (l == 0.f) ? 1.f : l;
+        const float inv_l = 1.f / l_safe;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(t_o + c * 32, r);
           tmem_ld_wait();
-          if (valid) {
-            float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float4 a = first ? make_float4(0.f, 0.f, 0.f, 0.f) : d4[e];
-              d4[e] = make_float4(fmaf(a.x, ca, __uint_as_float(r[4 * e + 0]) * cb),
-                                  fmaf(a.y, ca, __uint_as_float(r[4 * e + 1]) * cb),
-                                  fmaf(a.z, ca, __uint_as_float(r[4 * e + 2]) * cb),
-                                  fmaf(a.w, ca, __uint_as_float(r[4 * e + 3]) * cb));
-            }
-          }
+          stage_row32_sw128(o_tile, row, 32 * c, r, inv_l);
         }
-        if (valid) ACC_LSE[idx] = (mm == -INFINITY) ? -INFINITY : mm + log2f(wa + wb);
+        if (LSE != nullptr && grow < S) {
+          const float m_fin = (m_used == -INFINITY) ? 0.f : m_used;
+          LSE[static_cast<long long>(bh) * S + grow] = m_fin + __log2f(l_safe);
+        }
       }
-    } else if (staged) {
-      tc_fence_after();
-      const float l_safe = (l == 0.f) ? 1.f : l;
-      const float inv_l = 1.f / l_safe;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_o + c * 32, r);
-        tmem_ld_wait();
-        stage_row32_sw128(o_tile, row, 32 * c, r, inv_l);
-      }
-      if (LSE != nullptr && grow < S) {
-        const float m_fin = (m_used == -INFINITY) ? 0.f : m_used;
-        LSE[static_cast<long long>(bh) * S + grow] = m_fin + __log2f(l_safe);
-      }
-    }
-    fence_proxy_async_smem();
-    if (named_barrier_and(1 + i, 128, staged && !MERGE) && row == 0) {
+      fence_proxy_async_smem();
+      const bool store = named_barrier_and(1 + i, 128, staged && !MERGE);
+      if (row == 0) {
+        if (store) {
 #pragma unroll
-      for (int sl = 0; sl < SLABS; ++sl) tma_store_3d(&tm_o, o_tile + sl * 16384, sl * 64, mi, bh);
-      bulk_commit_group();
-      bulk_wait_read();
+          for (int sl = 0; sl < SLABS; ++sl) tma_store_3d(&tm_o, o_tile + sl * 16384, sl * 64, mi, bh);
+          bulk_commit_group();
+          bulk_wait_read();
+        }
+        mbar_arrive(q_empty(n & 1));  // this tile's half of the Q buffer may be reloaded
+      }
     }
   }
 
@@ -531,7 +577,6 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  FFA_FWD_CTA_TRACE(1, n_kv);
 }
 
 // ------------------------------------------------------------------------------------
@@ -539,7 +584,8 @@ __global__ void __launch_bounds__(fwd::NTHREADS, 1)
 // ------------------------------------------------------------------------------------
 template <int D, bool CAUSAL, bool MERGE>
 static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
-  using L = fwd::Layout<D>;
+  constexpr bool PERSIST = !MERGE && !fwd::seq_turns<D>();
+  using L = fwd::Layout<D, PERSIST>;
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_tile_map(&tq, a.q, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
@@ -547,7 +593,7 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if ((rc = make_tile_map(&tv, a.v, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
   CUtensorMap to;  // merge mode stores nothing through it: q serves as its base
   if ((rc = make_tile_map(&to, a.acc ? a.q : a.o, a.BH, a.S, D, a.stride_bh, a.stride_s)) != 0) return rc;
-  auto kern = ffa_fwd_kernel<D, CAUSAL, MERGE>;
+  auto kern = ffa_fwd_kernel<D, CAUSAL, MERGE, PERSIST>;
   static unsigned long long configured = 0;  // devices with the smem limit raised
   if ((rc = set_smem_once(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, &configured)) != 0) return rc;
   // The setmaxnreg split assumes the kernel is launched with 168 registers per thread;
@@ -562,7 +608,9 @@ static int launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if (launch_regs < fwd::LAUNCH_REGS_NEEDED)
     return set_error(FFA_ERR_LAUNCH, "forward kernel compiled with too few registers for its setmaxnreg split");
   const int n_mblk = (a.S + 2 * fwd::BM - 1) / (2 * fwd::BM);
-  const dim3 grid(static_cast<unsigned>(n_mblk) * static_cast<unsigned>(a.BH));
+  // PERSIST: one CTA per pair of blocks of a slice
+  const int n_rows = PERSIST ? (n_mblk + 1) / 2 : n_mblk;
+  const dim3 grid(static_cast<unsigned>(n_rows) * static_cast<unsigned>(a.BH));
   kern<<<grid, fwd::NTHREADS, L::SMEM_BYTES, stream>>>(tq, tk, tv, to, a.lse, a.S, a.BH, work_group(a.BH, a.S, D, CAUSAL),
                                                         static_cast<float>(a.scale * kLog2e), a.acc, a.acc_lse,
                                                         a.first);
