@@ -42,7 +42,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch of the dK/dV kernel, from one ncu capture of that
 # kernel at B2 H16 S8192 D128 causal (32 slices; dram__bytes_read.sum + dram__bytes_write.sum),
 # scaled to the bench's (batch, head) slice count: traffic grows in proportion to slices.
-DKDV_DRAM_BYTES_PER_SLICE = (284.761088e6 + 109.198592e6) / 32
+DKDV_DRAM_BYTES_PER_SLICE = (284.571648e6 + 106.757120e6) / 32
 
 
 def attn_flops(B, H, S, D, causal):
