@@ -755,7 +755,7 @@ def main():
     ap.add_argument("--S", type=int, default=8192)
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-chunks", type=int, default=8, help="head chunks (streams) of the pipelined e2e step")
+    ap.add_argument("--e2e-chunks", type=int, default=16, help="head chunks (streams) of the pipelined e2e step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-box", action="store_true", help="skip the B8 H32 global-problem (configs[3]) figure")
     ap.add_argument("--noncausal", action="store_true", help="--mode once: no causal mask")
